@@ -1,0 +1,379 @@
+"""Benchmark of the ExFold routing transform on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Default workload (the 48-layer sharded run): each GPU routes and folds T = 131072 tokens per
+layer through 48 Qwen3-shaped MoE layers (E = 128, top-8, keep P = 4, independent per-layer
+calibration tables), so per-GPU work is fixed as N grows (weak scaling; prefill needs no
+communication).  One step = 48 launches of the fused router + prefill-fold kernel, one per layer
+as a model calls it, replayed from a CUDA graph.  The 3.2 GB of logits per step are larger than
+L2, so no flush is needed between steps.  Rank 0 prints one JSON line.
+
+--impl reference runs the reference's CPU path for the same metric: the CPU oracle (a scalar C
+port of exfold/qwen3/kernels.py with the softmax/top-k router) on all host threads over a
+bounded sample of the same workload; under torchrun only rank 0 works.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "exfold-moe_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+
+LAYERS, TOKENS, EXPERTS, TOP_K, KEEP = 48, 131072, 128, 8, 4
+
+
+def bytes_per_launch(tokens: int) -> int:
+    """Algorithmic HBM bytes of one router + fold launch: logits in, P ids + P weights out, and
+    the coefficient and loss tables once."""
+    return tokens * (EXPERTS * 4 + KEEP * 8) + 2 * EXPERTS * EXPERTS * 4
+
+
+def set_shape(layers: int, tokens: int) -> None:
+    global LAYERS, TOKENS
+    LAYERS, TOKENS = layers, tokens
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profiled_traffic(name: str):
+    path = ROOT / "profiles" / "traffic.json"
+    if path.is_file():
+        return json.loads(path.read_text()).get(name)
+    return None
+
+
+# ---- clocks sampled during the timed region (NVML; read-only) ---------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            try:
+                p = torch.cuda.get_device_properties(device_index)
+                bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:  # noqa: BLE001
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = self._reasons(self._h)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        names = [n for b, n in _REASONS.items() if bits & b and b != 0x1]
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ---- workload ---------------------------------------------------------------------------------
+def qwen3_tables(layers: int):
+    """Per-layer calibration tables, prepared as exfold/qwen3/vllm_patch.py:59-61 prepares them."""
+    from exfold_b200 import calibration
+    from exfold_b200 import workloads as W
+
+    cfg = W.WORKLOADS["qwen3_layers"]
+    coeff, loss, norms = [], [], []
+    for layer in range(layers):
+        seed = cfg["seed"] + layer
+        coeff.append(W.coefficient(seed, EXPERTS, 0.35, 0.15))
+        loss.append(W.loss_matrix(seed, EXPERTS, 0.2, 1.0))
+        norms.append(W.expert_norms(seed, EXPERTS))
+    # the synthetic loss has a +inf diagonal, which the artifact check would reject
+    return calibration.prepare_qwen3(np.stack(coeff), np.stack(loss), np.stack(norms),
+                                     validate=False)
+
+
+def cpu_oracle_rate(logits: np.ndarray, coeff: np.ndarray, loss: np.ndarray, threads: int,
+                    budget_s: float) -> tuple[float, int]:
+    """Tokens/s of the CPU oracle (router + fold) on `threads` host threads; ctypes releases the
+    GIL, so threads run the C code in parallel.  Repeats the sample until budget_s is spent."""
+    from oracle import oracle as O
+
+    chunks = np.array_split(np.arange(logits.shape[0]), threads)
+
+    def work(idx):
+        O.router_fold(logits[idx], TOP_K, KEEP, coeff, loss)
+
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        while True:
+            list(ex.map(work, chunks))
+            done += logits.shape[0]
+            if time.perf_counter() - t0 >= budget_s:
+                break
+    return done / (time.perf_counter() - t0), done
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from exfold_b200 import workloads as W
+
+    threads = len(os.sched_getaffinity(0))
+    coeff, loss, _ = qwen3_tables(1)
+    sample = W.logits(W.WORKLOADS["qwen3_layers"]["seed"], 16384, EXPERTS)
+    rate, _ = cpu_oracle_rate(sample, coeff[0], loss[0], threads, 1.0)  # warm-up
+    # whole run bounded to ~2 minutes: at most 0.25 s of CPU work per step
+    step_s = min(0.25, 120.0 / (args.steps + args.warmup))
+    step_tokens = max(threads * 64, int(rate * step_s))
+    step_tokens = min(step_tokens, sample.shape[0])
+    sample = sample[:step_tokens]
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        cpu_oracle_rate(sample, coeff[0], loss[0], threads, 0.0)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = step_tokens * len(times) / total
+    line = {
+        "metric": "fold-transform tokens/s (router + prefill fold, 48 layers, T=131072/GPU, P=4)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic (seeded N(0,1) logits, seeded calibration tables)",
+        "config": {"workload": "qwen3_layers_prefill", "layers": LAYERS, "tokens_per_gpu": TOKENS,
+                   "experts": EXPERTS, "top_k": TOP_K, "keep": KEEP,
+                   "sample_tokens_per_step": step_tokens},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{step_tokens} tokens of layer 0 per step, split over "
+                                   f"{threads} threads"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm --------------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from exfold_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    coeff_np, loss_np, _ = qwen3_tables(LAYERS)
+    coeff = torch.from_numpy(coeff_np).to(dev)
+    loss = torch.from_numpy(loss_np).to(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4000 + 7919 * rank)
+    logits = torch.randn((LAYERS, TOKENS, EXPERTS), generator=gen, device=dev)
+    out_w = torch.empty((LAYERS, TOKENS, KEEP), dtype=torch.float32, device=dev)
+    out_ids = torch.empty((LAYERS, TOKENS, KEEP), dtype=torch.int32, device=dev)
+
+    def step():
+        for layer in range(LAYERS):
+            ops.router_fold_prefill(logits[layer], TOP_K, KEEP, coeff[layer], loss[layer],
+                                    out=(out_w[layer], out_ids[layer]))
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        step()  # eager warm-up (grid sizing queries happen outside capture)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.cuda.stream(stream):
+        with ClockSampler(local) as clocks:
+            ms = timed(graph.replay, args.steps)
+    ms_per_step = ms / args.steps
+    tokens_per_step = LAYERS * TOKENS * world
+    value = tokens_per_step / (ms_per_step / 1e3)
+    launch_s = ms_per_step / 1e3 / LAYERS
+    peaks = measured_peaks()
+    achieved = bytes_per_launch(TOKENS) / launch_s / 1e9
+
+    # layer-batched variant: one launch over all 48 layers
+    def batched():
+        ops.router_fold_prefill(logits, TOP_K, KEEP, coeff, loss, out=(out_w, out_ids))
+
+    with torch.cuda.stream(stream):
+        batched()
+        torch.cuda.synchronize(dev)
+        gb = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gb, stream=stream):
+            batched()
+        ms_b = timed(gb.replay, max(1, args.steps // 4)) / max(1, args.steps // 4)
+
+    # end to end through the public API: pinned host logits in, pinned host results out
+    slots = min(4, LAYERS)
+    host_in = torch.empty((slots, TOKENS, EXPERTS), dtype=torch.float32).pin_memory()
+    host_in.copy_(logits[:slots].cpu())
+    host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
+    host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
+    dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.float32, device=dev)
+
+    def e2e_step():
+        for layer in range(LAYERS):
+            buf = dev_in[layer % 2]
+            buf.copy_(host_in[layer % slots], non_blocking=True)
+            w, i = ops.router_fold_prefill(buf, TOP_K, KEEP, coeff[layer], loss[layer])
+            host_w[layer % slots].copy_(w, non_blocking=True)
+            host_i[layer % slots].copy_(i, non_blocking=True)
+
+    e2e_steps = max(2, min(10, args.steps // 100))
+    saved_warmup = args.warmup
+    args.warmup = 1
+    with torch.cuda.stream(stream):
+        ms_e2e = timed(e2e_step, e2e_steps) / e2e_steps
+    args.warmup = saved_warmup
+    h2d = LAYERS * TOKENS * EXPERTS * 4
+    d2h = LAYERS * TOKENS * KEEP * 8
+
+    cpu = None
+    if rank == 0 and world == 1:
+        sample = logits[0, :8192].cpu().numpy()
+        rate, done = cpu_oracle_rate(sample, coeff_np[0], loss_np[0], 1, 10.0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{done} tokens (8192-token slices of layer 0), single thread, ~10 s"}
+
+    if rank == 0:
+        line = {
+            "metric": "fold-transform tokens/s (router + prefill fold, 48 layers, T=131072/GPU, P=4)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) logits, seeded calibration tables)",
+            "config": {"workload": "qwen3_layers_prefill", "layers": LAYERS,
+                       "tokens_per_gpu": TOKENS, "experts": EXPERTS, "top_k": TOP_K,
+                       "keep": KEEP, "parallelism": f"token-sharded x{world}",
+                       "l2": "inputs 3.2 GB/step per GPU > L2, no flush"},
+            "gpu_launches": LAYERS * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": profiled_traffic("router_fold_qwen3_layer"),
+                         "peak_source": peaks["source"],
+                         "kernel": "exf::router_kernel<128, softmax, qwen3 fold>",
+                         "bytes_per_launch": bytes_per_launch(TOKENS),
+                         "us_per_launch": launch_s * 1e6},
+            "layer_batched": {"ms_per_step": ms_b, "tokens_per_s": tokens_per_step / (ms_b / 1e3),
+                              "launches_per_step": 1},
+            "e2e": {"value": tokens_per_step / (ms_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph, gb
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="smaller cases for profiling")
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="smaller cases for profiling")
+    args = ap.parse_args()
+    set_shape(args.layers, args.tokens)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

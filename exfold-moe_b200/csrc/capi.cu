@@ -1,0 +1,296 @@
+// extern "C" entry points of libexfold_b200.so: argument checks, error reporting, dispatch.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+
+#include "exf_common.cuh"
+#include "exf_kernels.h"
+#include "exf_launch.h"
+
+namespace exf {
+
+
+
+// ---- launch helpers -----------------------------------------------------------------------
+static std::mutex g_grid_mu;
+static std::unordered_map<uint64_t, int> g_grid_cache;
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+int persistent_grid(const void* kernel, int threads, size_t smem) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) << 8) ^ (uint64_t)dev;
+  {
+    std::lock_guard<std::mutex> lk(g_grid_mu);
+    auto it = g_grid_cache.find(key);
+    if (it != g_grid_cache.end()) return it->second;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess)
+    return 0;
+  const int grid = per_sm * sm_count();
+  std::lock_guard<std::mutex> lk(g_grid_mu);
+  g_grid_cache[key] = grid;
+  return grid;
+}
+
+}  // namespace exf
+
+using namespace exf;
+
+// ---- error reporting ------------------------------------------------------------------------
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) {
+    g_err[0] = 0;
+    return EXF_OK;
+  }
+  if (e == cudaErrorNotSupported) return fail(EXF_ERR_UNSUPPORTED, "%s: shape not compiled", what);
+  return fail(EXF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define EXF_REQUIRE(cond, ...)                                 \
+  do {                                                         \
+    if (!(cond)) return fail(EXF_ERR_INVALID, __VA_ARGS__);    \
+  } while (0)
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool good_wdtype(int d) { return d == EXF_F32 || d == EXF_BF16 || d == EXF_F16; }
+static bool good_idtype(int d) { return d == EXF_I32 || d == EXF_I64; }
+
+// ---- entry points ---------------------------------------------------------------------------
+extern "C" {
+
+EXF_API int exf_abi_version(void) { return 1; }
+
+EXF_API const char* exf_last_error(void) { return g_err; }
+
+static int router_common(const char* name, const float* logits, int64_t tokens, int layers,
+                         int experts, int top_k, int scoring, const float* out_w,
+                         const int32_t* out_ids) {
+  EXF_REQUIRE(tokens >= 0 && layers >= 1, "%s: tokens must be >= 0 and layers >= 1", name);
+  EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
+  EXF_REQUIRE(experts >= top_k, "%s: experts (%d) < top_k (%d)", name, experts, top_k);
+  EXF_REQUIRE(scoring == EXF_SOFTMAX || scoring == EXF_SIGMOID, "%s: unknown scoring %d", name,
+              scoring);
+  if (experts != 64 && experts != 128 && experts != 256 && experts != 512)
+    return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be one of 64, 128, 256, 512 (got %d)", name,
+                experts);
+  if (tokens > 0) {
+    EXF_REQUIRE(logits && out_w && out_ids, "%s: null pointer", name);
+    EXF_REQUIRE(aligned16(logits), "%s: logits must be 16-byte aligned", name);
+  }
+  return EXF_OK;
+}
+
+EXF_API int exf_router_topk(const float* logits, int64_t tokens, int experts, int top_k,
+                            int scoring, const float* bias, int renormalize, float scaling,
+                            float* out_w, int32_t* out_ids, exf_stream_t stream) {
+  int rc = router_common("exf_router_topk", logits, tokens, 1, experts, top_k, scoring, out_w,
+                         out_ids);
+  if (rc != EXF_OK) return rc;
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(!bias || aligned16(bias), "exf_router_topk: bias must be 16-byte aligned");
+  RouterParams p{logits, tokens, 1, top_k, bias, renormalize, scaling, top_k, 0,
+                 nullptr, nullptr, nullptr, out_w, out_ids};
+  return cuda_status(launch_router(experts, scoring, 0, p, (cudaStream_t)stream), "exf_router_topk");
+}
+
+EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int layers, int experts,
+                                    int top_k, int scoring, const float* bias, int renormalize,
+                                    float scaling, int target_k, int variant, int renorm_mode,
+                                    const float* coeff, const float* sel_loss,
+                                    const float* conf_loss, float* out_w, int32_t* out_ids,
+                                    exf_stream_t stream) {
+  const char* name = "exf_router_fold_prefill";
+  int rc = router_common(name, logits, tokens, layers, experts, top_k, scoring, out_w, out_ids);
+  if (rc != EXF_OK) return rc;
+  EXF_REQUIRE(variant == EXF_QWEN3 || variant == EXF_DSV4, "%s: unknown variant %d", name, variant);
+  EXF_REQUIRE(target_k >= 1 && target_k <= top_k, "%s: target_k must be in [1, top_k]", name);
+  EXF_REQUIRE(renorm_mode >= 0 && renorm_mode <= 2, "%s: renorm_mode must be 0, 1 or 2", name);
+  EXF_REQUIRE(variant == EXF_DSV4 || renorm_mode == 0, "%s: renorm_mode needs EXF_DSV4", name);
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(coeff && sel_loss, "%s: null calibration table", name);
+  EXF_REQUIRE(renorm_mode != 2 || conf_loss, "%s: similarity_blend needs conf_loss", name);
+  EXF_REQUIRE(!bias || aligned16(bias), "%s: bias must be 16-byte aligned", name);
+  RouterParams p{logits, tokens, layers, top_k, bias, renormalize, scaling, target_k, renorm_mode,
+                 coeff, sel_loss, conf_loss, out_w, out_ids};
+  return cuda_status(launch_router(experts, scoring, variant == EXF_QWEN3 ? 1 : 2, p,
+                                   (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int exf_fold_prefill(const void* w, int w_dtype, const void* ids, int id_dtype,
+                             int64_t tokens, int top_k, int target_k, int experts, int variant,
+                             int renorm_mode, const float* coeff, const float* sel_loss,
+                             const float* conf_loss, void* out_w, void* out_ids,
+                             exf_stream_t stream) {
+  const char* name = "exf_fold_prefill";
+  EXF_REQUIRE(good_wdtype(w_dtype) && good_idtype(id_dtype), "%s: unsupported dtype", name);
+  EXF_REQUIRE(tokens >= 0, "%s: tokens must be >= 0", name);
+  EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
+  EXF_REQUIRE(target_k >= 1 && target_k <= top_k, "%s: target_k must be in [1, top_k]", name);
+  EXF_REQUIRE(experts >= 1, "%s: experts must be >= 1", name);
+  EXF_REQUIRE(variant == EXF_QWEN3 || variant == EXF_DSV4, "%s: unknown variant %d", name, variant);
+  EXF_REQUIRE(renorm_mode >= 0 && renorm_mode <= 2, "%s: renorm_mode must be 0, 1 or 2", name);
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(w && ids && out_w && out_ids && coeff && sel_loss, "%s: null pointer", name);
+  EXF_REQUIRE(variant != EXF_DSV4 || renorm_mode != 2 || conf_loss,
+              "%s: similarity_blend needs conf_loss", name);
+  FoldParams p{w, ids, tokens, top_k, target_k, experts, variant == EXF_DSV4 ? renorm_mode : 0,
+               coeff, sel_loss, conf_loss, out_w, out_ids};
+  return cuda_status(launch_fold(w_dtype, id_dtype, variant, p, (cudaStream_t)stream), name);
+}
+
+static int decode_checks(const char* name, int w_dtype, int id_dtype, int64_t batch, int top_k,
+                         int experts, int budget, int variant) {
+  EXF_REQUIRE(good_wdtype(w_dtype) && good_idtype(id_dtype), "%s: unsupported dtype", name);
+  EXF_REQUIRE(batch >= 0 && top_k >= 1, "%s: bad routing shape", name);
+  EXF_REQUIRE(experts >= 1 && experts <= 1024, "%s: experts must be in [1, 1024]", name);
+  EXF_REQUIRE(budget >= 1 && budget <= experts, "%s: budget must be in [1, experts]", name);
+  EXF_REQUIRE(variant == EXF_QWEN3 || variant == EXF_DSV4, "%s: unknown variant %d", name, variant);
+  return EXF_OK;
+}
+
+EXF_API int exf_decode(const void* w, int w_dtype, const void* ids, int id_dtype, int64_t batch,
+                       int top_k, int experts, int budget, int variant, const float* norms,
+                       const float* coeff, const float* loss, void* out_w, void* out_ids,
+                       int32_t* out_subset, exf_stream_t stream) {
+  const char* name = "exf_decode";
+  int rc = decode_checks(name, w_dtype, id_dtype, batch, top_k, experts, budget, variant);
+  if (rc != EXF_OK) return rc;
+  EXF_REQUIRE(norms && coeff && loss, "%s: null calibration table", name);
+  EXF_REQUIRE(batch == 0 || (w && ids && out_w && out_ids), "%s: null routing pointer", name);
+  DecodeParams p{w, ids, batch * top_k, experts, budget, variant, 0 /*from routes*/, norms,
+                 nullptr, nullptr, coeff, loss, out_w, out_ids, out_subset};
+  return cuda_status(launch_decode(w_dtype, id_dtype, p, (cudaStream_t)stream), name);
+}
+
+EXF_API int exf_decode_importance(const void* w, int w_dtype, const void* ids, int id_dtype,
+                                  int64_t routes, int experts, const float* norms,
+                                  int64_t* importance, exf_stream_t stream) {
+  const char* name = "exf_decode_importance";
+  EXF_REQUIRE(good_wdtype(w_dtype) && good_idtype(id_dtype), "%s: unsupported dtype", name);
+  EXF_REQUIRE(routes >= 0 && experts >= 1 && experts <= 1024, "%s: bad shape", name);
+  EXF_REQUIRE(norms && importance, "%s: null pointer", name);
+  if (routes == 0) return EXF_OK;
+  EXF_REQUIRE(w && ids, "%s: null routing pointer", name);
+  return cuda_status(launch_importance(w_dtype, id_dtype, w, ids, routes, experts, norms,
+                                       importance, (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int exf_decode_apply(const int64_t* importance, const void* w, int w_dtype,
+                             const void* ids, int id_dtype, int64_t batch, int top_k,
+                             int experts, int budget, int variant, const float* coeff,
+                             const float* loss, void* out_w, void* out_ids, int32_t* out_subset,
+                             exf_stream_t stream) {
+  const char* name = "exf_decode_apply";
+  int rc = decode_checks(name, w_dtype, id_dtype, batch, top_k, experts, budget, variant);
+  if (rc != EXF_OK) return rc;
+  EXF_REQUIRE(importance && coeff && loss, "%s: null pointer", name);
+  EXF_REQUIRE(batch == 0 || (w && ids && out_w && out_ids), "%s: null routing pointer", name);
+  DecodeParams p{w, ids, batch * top_k, experts, budget, variant, 1 /*importance given*/,
+                 nullptr, importance, nullptr, coeff, loss, out_w, out_ids, out_subset};
+  return cuda_status(launch_decode(w_dtype, id_dtype, p, (cudaStream_t)stream), name);
+}
+
+EXF_API int exf_reroute_subset(const void* w, int w_dtype, const void* ids, int id_dtype,
+                               int64_t batch, int top_k, int experts, const int32_t* subset,
+                               int subset_size, const float* coeff, const float* loss,
+                               void* out_w, void* out_ids, exf_stream_t stream) {
+  const char* name = "exf_reroute_subset";
+  EXF_REQUIRE(subset_size >= 1 && subset_size <= experts, "%s: subset_size must be in [1, experts]",
+              name);
+  int rc = decode_checks(name, w_dtype, id_dtype, batch, top_k, experts, subset_size, EXF_QWEN3);
+  if (rc != EXF_OK) return rc;
+  EXF_REQUIRE(subset && coeff && loss, "%s: null pointer", name);
+  if (batch == 0) return EXF_OK;
+  EXF_REQUIRE(w && ids && out_w && out_ids, "%s: null routing pointer", name);
+  DecodeParams p{w, ids, batch * top_k, experts, subset_size, EXF_QWEN3, 2 /*subset given*/,
+                 nullptr, nullptr, subset, coeff, loss, out_w, out_ids, nullptr};
+  return cuda_status(launch_decode(w_dtype, id_dtype, p, (cudaStream_t)stream), name);
+}
+
+EXF_API int exf_static_table(const float* norms, const float* coeff, const float* loss,
+                             int experts, int budget, int32_t* target, float* scale,
+                             exf_stream_t stream) {
+  const char* name = "exf_static_table";
+  EXF_REQUIRE(experts >= 1 && experts <= 1024, "%s: experts must be in [1, 1024]", name);
+  EXF_REQUIRE(budget >= 1 && budget <= experts, "%s: budget must be in [1, experts]", name);
+  EXF_REQUIRE(norms && coeff && loss && target && scale, "%s: null pointer", name);
+  return cuda_status(launch_static_table(norms, coeff, loss, experts, budget, target, scale,
+                                         (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int exf_static_remap(void* w, int w_dtype, void* ids, int id_dtype, int64_t routes,
+                             int experts, const int32_t* target, const float* scale,
+                             exf_stream_t stream) {
+  const char* name = "exf_static_remap";
+  EXF_REQUIRE(good_wdtype(w_dtype) && good_idtype(id_dtype), "%s: unsupported dtype", name);
+  EXF_REQUIRE(routes >= 0 && experts >= 1, "%s: bad shape", name);
+  if (routes == 0) return EXF_OK;
+  EXF_REQUIRE(w && ids && target && scale, "%s: null pointer", name);
+  return cuda_status(launch_static_remap(w_dtype, id_dtype, w, ids, routes, experts, target, scale,
+                                         (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int64_t exf_moe_align_capacity(int64_t numel, int experts, int block_size, int pad_sorted) {
+  if (numel < 0 || experts < 1 || block_size < 1) return -1;
+  int64_t cap = numel + (int64_t)experts * (block_size - 1);
+  if (pad_sorted) cap = (cap + block_size - 1) / block_size * block_size;
+  if (numel < experts && numel * block_size < cap) cap = numel * block_size;
+  return cap;
+}
+
+EXF_API int64_t exf_moe_align_workspace_bytes(int64_t numel, int experts) {
+  if (numel < 0 || experts < 1) return -1;
+  return align_workspace_bytes(numel, experts);
+}
+
+EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int experts,
+                          int block_size, int64_t capacity, int32_t* sorted_ids,
+                          int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
+                          int64_t workspace_bytes, exf_stream_t stream) {
+  const char* name = "exf_moe_align";
+  EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported id dtype", name);
+  EXF_REQUIRE(numel >= 0 && numel < (int64_t)1 << 31, "%s: numel out of range", name);
+  EXF_REQUIRE(block_size >= 1, "%s: block_size must be >= 1", name);
+  if (experts < 1 || experts > align_max_experts())
+    return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
+  EXF_REQUIRE(capacity >= exf_moe_align_capacity(numel, experts, block_size, 0) ||
+                  capacity >= numel * (int64_t)block_size,
+              "%s: capacity too small", name);
+  EXF_REQUIRE(num_post_pad && (capacity == 0 || (sorted_ids && expert_ids)), "%s: null output",
+              name);
+  EXF_REQUIRE(numel == 0 || ids, "%s: null ids", name);
+  const int64_t need = align_workspace_bytes(numel, experts);
+  EXF_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
+              "%s: workspace of %lld bytes required", name, (long long)need);
+  AlignParams p{ids, numel, experts, block_size, capacity, sorted_ids, expert_ids, num_post_pad,
+                static_cast<int32_t*>(workspace), 0};
+  return cuda_status(launch_align(id_dtype, p, (cudaStream_t)stream), name);
+}
+
+}  // extern "C"

@@ -1,0 +1,371 @@
+// Decode expert budget kernels (sm_100a).
+//
+// decode_kernel is one CTA of 1024 threads doing the whole transform for a decode batch:
+//   1. importance[e] = sum over routes of w * norm[e] as 2^-32 fixed point in int64 (shared-
+//      memory 64-bit atomics: exact, so independent of the order the atomics land in), or
+//      read from a caller-reduced vector (batch sharded over GPUs), or skipped when the caller
+//      gives the subset explicitly;
+//   2. order = experts by (importance desc, expert asc), E/ (1024/E) comparisons per thread;
+//   3. per-expert target table: one warp per source expert, the subset's losses read from the
+//      L2-resident loss row by all 32 lanes, argmin by a (loss, position) shuffle reduction that
+//      reproduces the sequential strict-< scan of the reference;
+//   4. apply the table to every route.
+// A decode batch is at most a few thousand routes (B x k), so the single CTA keeps every phase
+// on chip and the transform costs one launch.
+// decode_importance_kernel is the multi-CTA first phase for a sharded or very large batch.
+#include <float.h>
+
+#include "exf_common.cuh"
+#include "exf_kernels.h"
+#include "exf_launch.h"
+
+namespace exf {
+
+constexpr int kDecodeThreads = 1024;
+constexpr int kMaxExperts = 1024;
+
+
+
+struct DecodeSmem {
+  long long imp[kMaxExperts];
+  int order[kMaxExperts];
+  int rank[kMaxExperts];
+  int tgt[kMaxExperts];
+  float scale[kMaxExperts];
+  unsigned char keep[kMaxExperts];
+};
+
+// Sequential strict-< argmin semantics as a (value, position) reduction.
+//   Qwen3 (exfold/qwen3/kernels.py:186-212): start from position 0; later NaNs never win, so
+//   NaN -> +inf, ties -> first position; a NaN at position 0 wins outright.
+//   DeepSeek-V4 (exfold_kernels.cu:175-187): start from FLT_MAX; only values strictly below
+//   FLT_MAX qualify; positions of non-positive importance are skipped.
+__device__ __forceinline__ void argmin_merge(float& v, int& pos, float ov, int opos) {
+  if (ov < v || (ov == v && opos < pos)) {
+    v = ov;
+    pos = opos;
+  }
+}
+
+template <typename WT, typename IT>
+__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeParams p) {
+  __shared__ DecodeSmem sm;
+  const int E = p.experts;
+  const int D = p.budget;
+  const int tid = threadIdx.x;
+  const WT* w = static_cast<const WT*>(p.w);
+  const IT* ids = static_cast<const IT*>(p.ids);
+
+  // ---- 1. importance ------------------------------------------------------------------------
+  for (int e = tid; e < E; e += kDecodeThreads) {
+    sm.imp[e] = (p.source == kImportanceGiven) ? p.importance[e] : 0;
+    sm.keep[e] = 0;
+  }
+  __syncthreads();
+  if (p.source == kImportanceFromRoutes) {
+    for (int64_t r = tid; r < p.routes; r += kDecodeThreads) {
+      const int e = (int)ids[r];
+      if (e < 0 || e >= E) continue;
+      const long long q = fixed_point(__fmul_rn(to_f32(w[r]), __ldg(p.norms + e)));
+      atomicAdd(reinterpret_cast<unsigned long long*>(&sm.imp[e]), (unsigned long long)q);
+    }
+    __syncthreads();
+  }
+
+  // ---- 2. order -------------------------------------------------------------------------------
+  if (p.source == kSubsetGiven) {
+    for (int e = tid; e < E; e += kDecodeThreads) sm.rank[e] = E;  // not in subset
+    __syncthreads();
+    for (int q = tid; q < D; q += kDecodeThreads) {
+      const int e = p.subset[q];
+      const bool ok = e >= 0 && e < E;
+      sm.order[q] = ok ? e : 0;  // an out-of-range subset entry never reads outside the tables
+      if (ok) sm.keep[e] = 1;
+    }
+  } else {
+    // threads per expert: TP consecutive lanes split the comparison loop
+    int tp = 1;
+    while (tp < 32 && tp * 2 * E <= kDecodeThreads) tp *= 2;
+    const int e = tid / tp;
+    const int sub = tid % tp;
+    int cnt = 0;
+    if (e < E) {
+      const long long ie = sm.imp[e];
+      for (int o = sub; o < E; o += tp) {
+        const long long io = sm.imp[o];
+        cnt += (io > ie || (io == ie && o < e)) ? 1 : 0;
+      }
+    }
+    for (int off = tp >> 1; off > 0; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off, tp);
+    if (e < E && sub == 0) {
+      sm.order[cnt] = e;
+      sm.rank[e] = cnt;
+    }
+    __syncthreads();
+    for (int e2 = tid; e2 < E; e2 += kDecodeThreads) {
+      const bool in_budget = sm.rank[e2] < D;
+      sm.keep[e2] = (p.variant == EXF_QWEN3) ? in_budget : (in_budget && sm.imp[e2] > 0);
+    }
+  }
+  __syncthreads();
+  if (p.out_subset) {
+    for (int q = tid; q < D; q += kDecodeThreads) p.out_subset[q] = sm.order[q];
+  }
+
+  // ---- 3. target table ----------------------------------------------------------------------
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  for (int e = warp; e < E; e += kDecodeThreads / 32) {
+    const float* lrow = p.loss + (int64_t)e * E;
+    int tgt = e;
+    float scale = 1.0f;
+    if (p.variant == EXF_QWEN3) {
+      float v = INFINITY;
+      int pos = 0x7fffffff;
+      for (int q = lane; q < D; q += 32) {
+        const float c = __ldg(lrow + sm.order[q]);
+        const float cv = (c != c) ? INFINITY : c;
+        if (cv < v) {
+          v = cv;
+          pos = q;
+        }
+      }
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+        const int op = __shfl_xor_sync(0xffffffffu, pos, off);
+        argmin_merge(v, pos, ov, op);
+      }
+      const float first = __ldg(lrow + sm.order[0]);
+      if (first != first || pos == 0x7fffffff) pos = 0;
+      tgt = sm.order[pos];
+      const float best = __ldg(lrow + tgt);
+      scale = (best < 1.0e30f) ? __ldg(p.coeff + (int64_t)e * E + tgt) : 0.0f;
+    } else if (!sm.keep[e] && sm.imp[e] > 0) {
+      float v = INFINITY;
+      int pos = 0x7fffffff;
+      for (int q = lane; q < D; q += 32) {
+        const int o = sm.order[q];
+        if (sm.imp[o] <= 0) continue;
+        const float c = __ldg(lrow + o);
+        if (c < FLT_MAX && c < v) {
+          v = c;
+          pos = q;
+        }
+      }
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+        const int op = __shfl_xor_sync(0xffffffffu, pos, off);
+        argmin_merge(v, pos, ov, op);
+      }
+      if (pos != 0x7fffffff) {
+        tgt = sm.order[pos];
+        scale = (tgt == e) ? 1.0f : __ldg(p.coeff + (int64_t)e * E + tgt);
+      }
+    }
+    if (lane == 0) {
+      sm.tgt[e] = tgt;
+      sm.scale[e] = scale;
+    }
+  }
+  __syncthreads();
+
+  // ---- 4. apply -----------------------------------------------------------------------------
+  WT* ow = static_cast<WT*>(p.out_w);
+  IT* oi = static_cast<IT*>(p.out_ids);
+  for (int64_t r = tid; r < p.routes; r += kDecodeThreads) {
+    const IT raw = ids[r];
+    const int e = (int)raw;
+    const WT wr = w[r];
+    if (e < 0 || e >= E) {
+      ow[r] = wr;
+      oi[r] = raw;
+    } else if (p.variant == EXF_QWEN3) {
+      if (sm.keep[e]) {
+        ow[r] = wr;
+        oi[r] = raw;
+      } else {
+        // exfold/qwen3/kernels.py:214-225: the scale is cast to the weight dtype first
+        const float s = to_f32(from_f32<WT>(sm.scale[e]));
+        ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr), s));
+        oi[r] = (IT)sm.tgt[e];
+      }
+    } else {
+      ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr), sm.scale[e]));
+      oi[r] = (IT)sm.tgt[e];
+    }
+  }
+}
+
+// Multi-CTA importance: per-CTA shared-memory histogram, then one 64-bit global atomic per
+// expert per CTA into the caller's (zeroed) vector.
+template <typename WT, typename IT>
+__global__ void __launch_bounds__(256) decode_importance_kernel(const void* wv, const void* idv,
+                                                                int64_t routes, int experts,
+                                                                const float* norms,
+                                                                int64_t* importance) {
+  __shared__ long long hist[kMaxExperts];
+  const WT* w = static_cast<const WT*>(wv);
+  const IT* ids = static_cast<const IT*>(idv);
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < routes;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const int e = (int)ids[r];
+    if (e < 0 || e >= experts) continue;
+    const long long q = fixed_point(__fmul_rn(to_f32(w[r]), __ldg(norms + e)));
+    atomicAdd(reinterpret_cast<unsigned long long*>(&hist[e]), (unsigned long long)q);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < experts; e += blockDim.x)
+    if (hist[e] != 0)
+      atomicAdd(reinterpret_cast<unsigned long long*>(importance + e), (unsigned long long)hist[e]);
+}
+
+// Static decode table (exfold/qwen3/vllm_patch.py:130-143): keep the `budget` experts of largest
+// calibrated norm, map every other expert to the kept expert of smallest loss.
+__global__ void __launch_bounds__(kDecodeThreads, 1) static_table_kernel(
+    const float* norms, const float* coeff, const float* loss, int E, int D, int32_t* target,
+    float* scale_out) {
+  __shared__ int order[kMaxExperts];
+  __shared__ int rank[kMaxExperts];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += kDecodeThreads) {
+    const uint32_t ke = key_of(__ldg(norms + e));
+    int cnt = 0;
+    for (int o = 0; o < E; ++o) cnt += ranks_before(key_of(__ldg(norms + o)), o, ke, e) ? 1 : 0;
+    order[cnt] = e;
+    rank[e] = cnt;
+  }
+  __syncthreads();
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  for (int e = warp; e < E; e += kDecodeThreads / 32) {
+    if (rank[e] < D) {
+      if (lane == 0) {
+        target[e] = e;
+        scale_out[e] = 1.0f;
+      }
+      continue;
+    }
+    const float* lrow = loss + (int64_t)e * E;
+    float v = INFINITY;
+    int pos = 0x7fffffff;
+    for (int q = lane; q < D; q += 32) {
+      const float c = __ldg(lrow + order[q]);
+      const float cv = (c != c) ? INFINITY : c;
+      if (cv < v) {
+        v = cv;
+        pos = q;
+      }
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const int op = __shfl_xor_sync(0xffffffffu, pos, off);
+      argmin_merge(v, pos, ov, op);
+    }
+    const float first = __ldg(lrow + order[0]);
+    if (first != first || pos == 0x7fffffff) pos = 0;
+    if (lane == 0) {
+      target[e] = order[pos];
+      scale_out[e] = __ldg(coeff + (int64_t)e * E + order[pos]);
+    }
+  }
+}
+
+// In-place remap (exfold/qwen3/kernels.py:295-319): ids = target[ids], w = w * scale[ids].
+template <typename WT, typename IT>
+__global__ void __launch_bounds__(256) static_remap_kernel(void* wv, void* idv, int64_t routes,
+                                                           int experts, const int32_t* target,
+                                                           const float* scale) {
+  WT* w = static_cast<WT*>(wv);
+  IT* ids = static_cast<IT*>(idv);
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < routes;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const int e = (int)ids[r];
+    if (e < 0 || e >= experts) continue;
+    w[r] = from_f32<WT>(__fmul_rn(to_f32(w[r]), __ldg(scale + e)));
+    ids[r] = (IT)__ldg(target + e);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename WT, typename IT>
+static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
+  decode_kernel<WT, IT><<<1, kDecodeThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s) {
+  const bool i32 = id_dtype == EXF_I32;
+  switch (w_dtype) {
+    case EXF_F32: return i32 ? launch_decode_t<float, int32_t>(p, s) : launch_decode_t<float, int64_t>(p, s);
+    case EXF_BF16:
+      return i32 ? launch_decode_t<__nv_bfloat16, int32_t>(p, s)
+                 : launch_decode_t<__nv_bfloat16, int64_t>(p, s);
+    default: return i32 ? launch_decode_t<__half, int32_t>(p, s) : launch_decode_t<__half, int64_t>(p, s);
+  }
+}
+
+template <typename WT, typename IT>
+static cudaError_t launch_importance_t(const void* w, const void* ids, int64_t routes, int experts,
+                                       const float* norms, int64_t* imp, cudaStream_t s) {
+  int64_t blocks = (routes + 255) / 256;
+  const int cap = 2 * sm_count();
+  if (cap > 0 && blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  decode_importance_kernel<WT, IT><<<(unsigned)blocks, 256, 0, s>>>(w, ids, routes, experts, norms, imp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,
+                              int64_t routes, int experts, const float* norms, int64_t* imp,
+                              cudaStream_t s) {
+  const bool i32 = id_dtype == EXF_I32;
+  switch (w_dtype) {
+    case EXF_F32:
+      return i32 ? launch_importance_t<float, int32_t>(w, ids, routes, experts, norms, imp, s)
+                 : launch_importance_t<float, int64_t>(w, ids, routes, experts, norms, imp, s);
+    case EXF_BF16:
+      return i32 ? launch_importance_t<__nv_bfloat16, int32_t>(w, ids, routes, experts, norms, imp, s)
+                 : launch_importance_t<__nv_bfloat16, int64_t>(w, ids, routes, experts, norms, imp, s);
+    default:
+      return i32 ? launch_importance_t<__half, int32_t>(w, ids, routes, experts, norms, imp, s)
+                 : launch_importance_t<__half, int64_t>(w, ids, routes, experts, norms, imp, s);
+  }
+}
+
+cudaError_t launch_static_table(const float* norms, const float* coeff, const float* loss, int E,
+                                int D, int32_t* target, float* scale, cudaStream_t s) {
+  static_table_kernel<<<1, kDecodeThreads, 0, s>>>(norms, coeff, loss, E, D, target, scale);
+  return cudaGetLastError();
+}
+
+template <typename WT, typename IT>
+static cudaError_t launch_remap_t(void* w, void* ids, int64_t routes, int experts,
+                                  const int32_t* target, const float* scale, cudaStream_t s) {
+  int64_t blocks = (routes + 255) / 256;
+  const int cap = 4 * sm_count();
+  if (cap > 0 && blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  static_remap_kernel<WT, IT><<<(unsigned)blocks, 256, 0, s>>>(w, ids, routes, experts, target, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_static_remap(int w_dtype, int id_dtype, void* w, void* ids, int64_t routes,
+                                int experts, const int32_t* target, const float* scale,
+                                cudaStream_t s) {
+  const bool i32 = id_dtype == EXF_I32;
+  switch (w_dtype) {
+    case EXF_F32:
+      return i32 ? launch_remap_t<float, int32_t>(w, ids, routes, experts, target, scale, s)
+                 : launch_remap_t<float, int64_t>(w, ids, routes, experts, target, scale, s);
+    case EXF_BF16:
+      return i32 ? launch_remap_t<__nv_bfloat16, int32_t>(w, ids, routes, experts, target, scale, s)
+                 : launch_remap_t<__nv_bfloat16, int64_t>(w, ids, routes, experts, target, scale, s);
+    default:
+      return i32 ? launch_remap_t<__half, int32_t>(w, ids, routes, experts, target, scale, s)
+                 : launch_remap_t<__half, int64_t>(w, ids, routes, experts, target, scale, s);
+  }
+}
+
+}  // namespace exf

@@ -1,0 +1,119 @@
+// Shared device helpers for the ExFold routing-transform kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "exfold_b200.h"
+
+namespace exf {
+
+// ---------------------------------------------------------------------------------------------
+// Element types of the routing tensors.  Computation is fp32; weights are read and written in
+// their own type, ids as int32 or int64.
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// ---------------------------------------------------------------------------------------------
+// Exact elementwise math.  These functions are defined by their operation sequence: every step
+// is one IEEE binary32 operation with round-to-nearest-even (explicit _rn intrinsics, no
+// contraction), so a scalar C restatement performing the same steps returns the same bits.
+//
+// exp(x): Cody-Waite reduction x = n*ln2 + r with ln2 split into a 15-bit head (n*ln2_hi exact)
+// and a tail, the degree-7 Taylor polynomial of e^r on |r| <= ln2/2 by Horner with fused
+// multiply-adds (truncation error below 6e-9 relative), and scaling by 2^n through the exponent
+// field.  Inputs are clamped to [-87, 88] (NaN to -87) so that 2^n stays a normal number.
+constexpr float kLog2e = 0x1.715476p+0f;
+constexpr float kLn2Hi = 0x1.62e4p-1f;
+constexpr float kLn2Lo = 0x1.7f7d1cp-20f;
+
+__device__ __forceinline__ float exact_exp(float x) {
+  x = (x > -87.0f) ? x : -87.0f;
+  x = (x > 88.0f) ? 88.0f : x;
+  const float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fmaf_rn(n, -kLn2Hi, x);
+  r = __fmaf_rn(n, -kLn2Lo, r);
+  float p = 0x1.a01a02p-13f;          // 1/7!
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);  // 1/6!
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);   // 1/5!
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);   // 1/4!
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);   // 1/3!
+  p = __fmaf_rn(p, r, 0x1p-1f);          // 1/2!
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = __float2int_rz(n);
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+__device__ __forceinline__ float exact_sigmoid(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exact_exp(-x)));
+}
+
+// Fast sigmoid used only to pre-select candidates; its error is far below kSigmoidMargin, and
+// every candidate is then re-ranked with exact_sigmoid.
+// fminf maps NaN to 88, matching exact_sigmoid (whose exp clamp sends NaN to sigmoid(88)).
+__device__ __forceinline__ float approx_sigmoid(float x) {
+  x = fminf(x, 88.0f);
+  return __fdividef(1.0f, 1.0f + __expf(-x));
+}
+// Bound on |approx_sigmoid(x) + b - (exact_sigmoid(x) + b)| with a wide safety factor.
+constexpr float kSigmoidMargin = 1.0e-4f;
+
+// Keys: floats mapped to unsigned ints in IEEE 754 totalOrder (-NaN < -inf < ... < -0 < +0 <
+// ... < +inf < +NaN), two instructions.  key_of additionally ranks -0 equal to +0, which is
+// the order every comparison of the reference sees for finite values.
+constexpr uint32_t kKeyPosZero = 0x80000000u;
+constexpr uint32_t kKeyNegZero = 0x7FFFFFFFu;
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t key_of(float x) {
+  const uint32_t k = order_key(x);
+  return k == kKeyNegZero ? kKeyPosZero : k;
+}
+__device__ __forceinline__ float float_of_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// (key desc, index asc) order
+__device__ __forceinline__ bool ranks_before(uint32_t ka, int ia, uint32_t kb, int ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+// Decode importance in 2^-32 fixed point: fp32 product, clamp to |p| <= 2^30, round to nearest
+// even.  Integer sums are exact, so the result does not depend on summation order or on how a
+// batch is split over GPUs.
+__device__ __forceinline__ long long fixed_point(float p) {
+  p = fminf(fmaxf(p, -1073741824.0f), 1073741824.0f);
+  return __float2ll_rn(__fmul_rn(p, 4294967296.0f));
+}
+
+// Streaming 16-byte load that does not allocate in L1 (router logits are read exactly once).
+__device__ __forceinline__ float4 ld_stream_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+}  // namespace exf

@@ -1,0 +1,91 @@
+// Kernel parameter blocks and host launchers (internal to libexfold_b200.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace exf {
+
+enum FoldKind { kFoldNone = 0, kFoldQwen3 = 1, kFoldDsv4 = 2 };
+
+struct RouterParams {
+  const float* logits;   // [layers][tokens][E]
+  int64_t tokens;        // per layer
+  int layers;
+  int top_k;
+  const float* bias;     // [layers][E] or null
+  int renormalize;
+  float scaling;
+  int target_k;
+  int renorm_mode;
+  const float* coeff;    // [layers][E][E]
+  const float* sel_loss;
+  const float* conf_loss;
+  float* out_w;          // [layers][tokens][top_k or target_k]
+  int32_t* out_ids;
+};
+
+struct FoldParams {
+  const void* w;
+  const void* ids;
+  int64_t tokens;
+  int top_k;
+  int target_k;
+  int experts;
+  int renorm_mode;
+  const float* coeff;
+  const float* sel_loss;
+  const float* conf_loss;
+  void* out_w;
+  void* out_ids;
+};
+
+enum DecodeSource { kImportanceFromRoutes = 0, kImportanceGiven = 1, kSubsetGiven = 2 };
+
+struct DecodeParams {
+  const void* w;
+  const void* ids;
+  int64_t routes;
+  int experts;
+  int budget;
+  int variant;
+  int source;
+  const float* norms;
+  const int64_t* importance;
+  const int32_t* subset;
+  const float* coeff;
+  const float* loss;
+  void* out_w;
+  void* out_ids;
+  int32_t* out_subset;
+};
+
+struct AlignParams {
+  const void* ids;
+  int64_t numel;
+  int experts;
+  int block_size;
+  int64_t capacity;
+  int32_t* sorted_ids;
+  int32_t* expert_ids;
+  int32_t* num_post_pad;
+  int32_t* table;  // [chunks][experts]
+  int64_t chunks;
+};
+
+cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p, cudaStream_t s);
+cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p, cudaStream_t s);
+cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s);
+cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,
+                              int64_t routes, int experts, const float* norms, int64_t* imp,
+                              cudaStream_t s);
+cudaError_t launch_static_table(const float* norms, const float* coeff, const float* loss, int E,
+                                int D, int32_t* target, float* scale, cudaStream_t s);
+cudaError_t launch_static_remap(int w_dtype, int id_dtype, void* w, void* ids, int64_t routes,
+                                int experts, const int32_t* target, const float* scale,
+                                cudaStream_t s);
+cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s);
+int64_t align_workspace_bytes(int64_t numel, int experts);
+int align_max_experts();
+
+}  // namespace exf

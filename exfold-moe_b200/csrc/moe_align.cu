@@ -1,0 +1,207 @@
+// moe_align / permute (sm_100a): group routes by expert, pad each expert to a multiple of the
+// GEMM block size, name each block's expert.  Routes of one expert keep ascending flat order
+// (a stable counting sort), so the permutation is deterministic.
+//
+// numel <= kAlignSmall: one CTA does count, scan and stable scatter in shared memory.
+// Larger: count (one CTA per 2048-route chunk, shared-memory histogram) -> scan (one CTA:
+// column prefix over chunks, padded exclusive scan over experts, padding and block->expert
+// fill) -> stable scatter (one CTA per chunk).  The [chunks][experts] int32 table lives in the
+// caller's workspace.
+#include "exf_common.cuh"
+#include "exf_kernels.h"
+#include "exf_launch.h"
+
+namespace exf {
+
+constexpr int kAlignThreads = 512;
+constexpr int kAlignWarps = kAlignThreads / 32;
+constexpr int kAlignMaxExperts = 512;
+constexpr int64_t kAlignChunk = 2048;
+constexpr int64_t kAlignSmall = 8192;
+
+
+struct AlignSmem {
+  int count[kAlignMaxExperts];
+  int base[kAlignMaxExperts];
+  int off[kAlignMaxExperts + 1];
+  int wcnt[kAlignWarps][kAlignMaxExperts];
+  int scan[kAlignThreads];
+};
+
+template <typename IT>
+__device__ __forceinline__ int expert_of(const IT* ids, int64_t r, int64_t end, int E) {
+  if (r >= end) return -1;
+  const int e = (int)ids[r];
+  return (e >= 0 && e < E) ? e : -1;
+}
+
+// Stable scatter of routes [start, end): base[e] holds the next slot of expert e.
+template <typename IT>
+__device__ void stable_scatter(const IT* ids, int64_t start, int64_t end, int E, AlignSmem& sm,
+                               int32_t* sorted_ids) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t s0 = start; s0 < end; s0 += kAlignThreads) {
+    const int64_t r = s0 + tid;
+    const int e = expert_of(ids, r, end, E);
+    for (int x = lane; x < E; x += 32) sm.wcnt[warp][x] = 0;
+    __syncwarp();
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    const int lane_rank = __popc(m & lt);
+    if (e >= 0 && lane_rank == 0) sm.wcnt[warp][e] = __popc(m);
+    __syncthreads();
+    if (e >= 0) {
+      int prefix = 0;
+      for (int w = 0; w < warp; ++w) prefix += sm.wcnt[w][e];
+      sorted_ids[sm.base[e] + prefix + lane_rank] = (int32_t)r;
+    }
+    __syncthreads();
+    for (int x = tid; x < E; x += kAlignThreads) {
+      int add = 0;
+      for (int w = 0; w < kAlignWarps; ++w) add += sm.wcnt[w][x];
+      sm.base[x] += add;
+    }
+    __syncthreads();
+  }
+}
+
+// Padded exclusive scan over experts (counts in sm.count) -> sm.off[0..E]; then padding, tail
+// and block -> expert fill.  Called by one CTA.
+__device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
+  const int tid = threadIdx.x;
+  const int E = p.experts;
+  const int BM = p.block_size;
+  // experts per thread: E <= kAlignMaxExperts == kAlignThreads, so one expert per thread
+  const int c = tid < E ? sm.count[tid] : 0;
+  const int padded = (c + BM - 1) / BM * BM;
+  sm.scan[tid] = padded;
+  __syncthreads();
+  for (int d = 1; d < kAlignThreads; d <<= 1) {
+    const int v = tid >= d ? sm.scan[tid - d] : 0;
+    __syncthreads();
+    sm.scan[tid] += v;
+    __syncthreads();
+  }
+  if (tid < E) sm.off[tid + 1] = sm.scan[tid];
+  if (tid == 0) sm.off[0] = 0;
+  __syncthreads();
+  const int total = sm.off[E];
+  if (tid < E) {
+    for (int q = sm.off[tid] + c; q < sm.off[tid] + padded; ++q) p.sorted_ids[q] = (int32_t)p.numel;
+  }
+  for (int64_t q = total + tid; q < p.capacity; q += kAlignThreads) p.sorted_ids[q] = (int32_t)p.numel;
+  const int64_t nblocks = (p.capacity + BM - 1) / BM;
+  const int used = total / BM;
+  for (int64_t b = tid; b < nblocks; b += kAlignThreads) {
+    int e = -1;
+    if (b < used) {
+      const int start = (int)b * BM;
+      int lo = 0, hi = E - 1;  // last expert with off[e] <= start
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sm.off[mid] <= start) lo = mid; else hi = mid - 1;
+      }
+      e = lo;
+    }
+    p.expert_ids[b] = e;
+  }
+  if (tid == 0) *p.num_post_pad = total;
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(kAlignThreads, 1) align_small_kernel(const AlignParams p) {
+  __shared__ AlignSmem sm;
+  const IT* ids = static_cast<const IT*>(p.ids);
+  const int tid = threadIdx.x;
+  for (int e = tid; e < p.experts; e += kAlignThreads) sm.count[e] = 0;
+  __syncthreads();
+  for (int64_t r = tid; r < p.numel; r += kAlignThreads) {
+    const int e = expert_of(ids, r, p.numel, p.experts);
+    if (e >= 0) atomicAdd(&sm.count[e], 1);
+  }
+  __syncthreads();
+  scan_and_fill(p, sm);
+  for (int e = tid; e < p.experts; e += kAlignThreads) sm.base[e] = sm.off[e];
+  __syncthreads();
+  stable_scatter(ids, 0, p.numel, p.experts, sm, p.sorted_ids);
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(kAlignThreads) align_count_kernel(const AlignParams p) {
+  __shared__ int hist[kAlignMaxExperts];
+  const IT* ids = static_cast<const IT*>(p.ids);
+  const int64_t start = (int64_t)blockIdx.x * kAlignChunk;
+  const int64_t end = min(start + kAlignChunk, p.numel);
+  for (int e = threadIdx.x; e < p.experts; e += kAlignThreads) hist[e] = 0;
+  __syncthreads();
+  for (int64_t r = start + threadIdx.x; r < end; r += kAlignThreads) {
+    const int e = expert_of(ids, r, end, p.experts);
+    if (e >= 0) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < p.experts; e += kAlignThreads)
+    p.table[(int64_t)blockIdx.x * p.experts + e] = hist[e];
+}
+
+__global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const AlignParams p) {
+  __shared__ AlignSmem sm;
+  const int tid = threadIdx.x;
+  const int E = p.experts;
+  if (tid < E) {
+    int run = 0;
+    for (int64_t b = 0; b < p.chunks; ++b) {
+      const int c = p.table[b * E + tid];
+      p.table[b * E + tid] = run;  // routes of expert tid in chunks before b
+      run += c;
+    }
+    sm.count[tid] = run;
+  }
+  __syncthreads();
+  scan_and_fill(p, sm);
+  if (tid < E) {
+    const int o = sm.off[tid];
+    for (int64_t b = 0; b < p.chunks; ++b) p.table[b * E + tid] += o;
+  }
+}
+
+template <typename IT>
+__global__ void __launch_bounds__(kAlignThreads, 1) align_scatter_kernel(const AlignParams p) {
+  __shared__ AlignSmem sm;
+  const IT* ids = static_cast<const IT*>(p.ids);
+  for (int e = threadIdx.x; e < p.experts; e += kAlignThreads)
+    sm.base[e] = p.table[(int64_t)blockIdx.x * p.experts + e];
+  __syncthreads();
+  const int64_t start = (int64_t)blockIdx.x * kAlignChunk;
+  const int64_t end = min(start + kAlignChunk, p.numel);
+  stable_scatter(ids, start, end, p.experts, sm, p.sorted_ids);
+}
+
+// ---------------------------------------------------------------------------------------------
+int64_t align_workspace_bytes(int64_t numel, int experts) {
+  if (numel <= kAlignSmall) return 0;
+  const int64_t chunks = (numel + kAlignChunk - 1) / kAlignChunk;
+  return chunks * experts * (int64_t)sizeof(int32_t);
+}
+
+int align_max_experts() { return kAlignMaxExperts; }
+
+template <typename IT>
+static cudaError_t launch_align_t(AlignParams p, cudaStream_t s) {
+  if (p.numel <= kAlignSmall) {
+    align_small_kernel<IT><<<1, kAlignThreads, 0, s>>>(p);
+    return cudaGetLastError();
+  }
+  p.chunks = (p.numel + kAlignChunk - 1) / kAlignChunk;
+  align_count_kernel<IT><<<(unsigned)p.chunks, kAlignThreads, 0, s>>>(p);
+  align_scan_kernel<<<1, kAlignThreads, 0, s>>>(p);
+  align_scatter_kernel<IT><<<(unsigned)p.chunks, kAlignThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s) {
+  return id_dtype == EXF_I32 ? launch_align_t<int32_t>(p, s) : launch_align_t<int64_t>(p, s);
+}
+
+}  // namespace exf

@@ -1,0 +1,591 @@
+// Router top-k and prefill fold kernels (sm_100a).
+//
+// router_kernel: one pass over the router logits per token, optionally fused with the ExFold
+// prefill fold, so the [tokens][top_k] routing tensors never reach HBM.
+//   * A token is owned by a group of L = E/32 lanes; each lane holds 32 logits in registers
+//     (8 coalesced 16-byte streaming loads) and stages them in shared memory.
+//   * Selection: the exact top-k set is contained in the candidates whose key is >= theta, where
+//     theta is the k-th largest maximum over groups of 4 consecutive keys (k distinct elements
+//     reach it, so the k-th largest key is >= theta).  theta comes from a register bitonic
+//     network over the group maxima (19-comparator sort per lane, then log2(L) shuffle merges).
+//     For the sigmoid router the network runs on fast approximate keys and theta is lowered by
+//     twice their error bound, which keeps the containment.  Candidates (typically 9-12 of the
+//     E experts) are ranked exactly by (key desc, expert asc); a token with more than
+//     kMaxCand candidates (ties, constant rows) takes an exact k-round selection instead.
+//   * Fold: omitted slots are spread over the group's lanes, their loss/scale gathers hit the
+//     L2-resident E x E tables, and the transfers are accumulated in slot order.
+// fold_kernel: the fold alone from precomputed top-k routes (one thread per token), for the
+//   reference-compatible API that receives (weights, ids).
+#include <float.h>
+
+#include "exf_common.cuh"
+#include "exf_kernels.h"
+#include "exf_launch.h"
+
+namespace exf {
+
+constexpr int kMaxK = 8;
+constexpr int kMaxCand = 32;
+
+
+template <int E>
+struct RouterShape {
+  static constexpr int L = E / 32;        // lanes per token
+  static constexpr int TPW = 32 / L;      // tokens per warp
+  static constexpr int WARPS = (E >= 128) ? 4 : 2;
+  static constexpr int ROW = E + 16;      // padded staging row (floats)
+};
+
+__device__ __forceinline__ void cx_desc(uint32_t& a, uint32_t& b) {
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+
+// Optimal 19-comparator network for 8 inputs, descending.
+__device__ __forceinline__ void sort8_desc(uint32_t (&v)[8]) {
+  cx_desc(v[0], v[2]); cx_desc(v[1], v[3]); cx_desc(v[4], v[6]); cx_desc(v[5], v[7]);
+  cx_desc(v[0], v[4]); cx_desc(v[1], v[5]); cx_desc(v[2], v[6]); cx_desc(v[3], v[7]);
+  cx_desc(v[0], v[1]); cx_desc(v[2], v[3]); cx_desc(v[4], v[5]); cx_desc(v[6], v[7]);
+  cx_desc(v[2], v[4]); cx_desc(v[3], v[5]);
+  cx_desc(v[1], v[4]); cx_desc(v[3], v[6]);
+  cx_desc(v[1], v[2]); cx_desc(v[3], v[4]); cx_desc(v[5], v[6]);
+}
+
+// a, b sorted descending -> a = the 8 largest of both, sorted descending.
+__device__ __forceinline__ void merge8_desc(uint32_t (&a)[8], const uint32_t (&b)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = max(a[i], b[7 - i]);
+  cx_desc(a[0], a[4]); cx_desc(a[1], a[5]); cx_desc(a[2], a[6]); cx_desc(a[3], a[7]);
+  cx_desc(a[0], a[2]); cx_desc(a[1], a[3]); cx_desc(a[4], a[6]); cx_desc(a[5], a[7]);
+  cx_desc(a[0], a[1]); cx_desc(a[2], a[3]); cx_desc(a[4], a[5]); cx_desc(a[6], a[7]);
+}
+
+
+template <int E>
+struct __align__(16) RouterSmem {
+  using S = RouterShape<E>;
+  static constexpr int CSTR = kMaxCand + 1;  // candidate rows: groups land on distinct banks
+  static constexpr int SSTR = 12;            // slot rows: 16-byte aligned, distinct bank quads
+  __align__(16) float vals[S::WARPS][S::TPW][S::ROW];
+  __align__(16) unsigned long long cand[S::WARPS][S::TPW][CSTR];  // key << 32 | ~expert
+  __align__(16) float cval[S::WARPS][S::TPW][CSTR];
+  __align__(16) int sidx[S::WARPS][S::TPW][SSTR];   // selected experts, router order
+  __align__(16) float sval[S::WARPS][S::TPW][SSTR]; // logit (softmax) / exact sigmoid
+  __align__(16) float sw[S::WARPS][S::TPW][SSTR];   // unnormalised weight
+  __align__(16) float wf[S::WARPS][S::TPW][SSTR];   // final weight, router order
+  __align__(16) int fidx[S::WARPS][S::TPW][SSTR];   // fold order (DeepSeek-V4: weight-sorted)
+  __align__(16) float fw[S::WARPS][S::TPW][SSTR];
+  __align__(16) int fpos[S::WARPS][S::TPW][SSTR];   // omitted slot -> retained position
+  __align__(16) float ft[S::WARPS][S::TPW][SSTR];   // omitted slot -> transfer
+  __align__(16) float ff[S::WARPS][S::TPW][SSTR];   // omitted slot -> lost mass (blend)
+  __align__(16) float acc[S::WARPS][S::TPW][SSTR];  // folded retained weights
+};
+
+template <int E, int SCORING, int FOLD>
+__global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
+    router_kernel(const RouterParams p) {
+  using S = RouterShape<E>;
+  constexpr int L = S::L;
+  constexpr int TPW = S::TPW;
+  __shared__ RouterSmem<E> sm;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane / L;
+  const int r = lane % L;
+  const unsigned gmask = (L == 32 ? 0xffffffffu : ((1u << L) - 1u)) << (g * L);
+  const int K = p.top_k;
+  const int P = p.target_k;
+  const int64_t total = (int64_t)p.layers * p.tokens;
+  const int64_t stride = (int64_t)gridDim.x * S::WARPS * TPW;
+
+  float* sv = sm.vals[warp][g];
+  unsigned long long* cand = sm.cand[warp][g];
+  float* cval = sm.cval[warp][g];
+  int* sidx = sm.sidx[warp][g];
+  float* sval = sm.sval[warp][g];
+  float* swt = sm.sw[warp][g];
+  float* wf = sm.wf[warp][g];
+
+  for (int64_t base = ((int64_t)blockIdx.x * S::WARPS + warp) * TPW; base < total; base += stride) {
+    const int64_t gt = base + g;
+    const bool valid = gt < total;
+    const int64_t layer = valid ? gt / p.tokens : 0;
+    const float* row = p.logits + (valid ? gt : 0) * E;
+    const float* brow = (SCORING == EXF_SIGMOID && p.bias) ? p.bias + layer * E : nullptr;
+
+    // ---- load, stage, selection keys (IEEE total order; exact logits or fast sigmoid) -------
+    uint32_t keys[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int col = 4 * (r + L * i);
+      float4 v = valid ? ld_stream_f4(row + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(sv + col) = v;
+      float x[4] = {v.x, v.y, v.z, v.w};
+      if (SCORING == EXF_SIGMOID) {
+        const float4 b = brow ? __ldg(reinterpret_cast<const float4*>(brow + col))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[0] = approx_sigmoid(x[0]) + b.x;
+        x[1] = approx_sigmoid(x[1]) + b.y;
+        x[2] = approx_sigmoid(x[2]) + b.z;
+        x[3] = approx_sigmoid(x[3]) + b.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) keys[4 * i + c] = order_key(x[c]);
+    }
+
+    // ---- threshold: k-th largest group-of-4 maximum over the token --------------------------
+    uint32_t top[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      top[i] = max(max(keys[4 * i], keys[4 * i + 1]), max(keys[4 * i + 2], keys[4 * i + 3]));
+    sort8_desc(top);
+#pragma unroll
+    for (int off = 1; off < L; off <<= 1) {
+      uint32_t other[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, top[i], off);
+      merge8_desc(top, other);
+    }
+    uint32_t theta = top[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i)
+      if (i == K - 1) theta = top[i];
+    if (SCORING == EXF_SIGMOID)
+      theta = order_key(float_of_key(theta) - 2.0f * kSigmoidMargin);
+    else if (theta == kKeyPosZero)
+      theta = kKeyNegZero;  // -0 ranks equal to +0
+
+    // ---- candidates ------------------------------------------------------------------------
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= (keys[j] >= theta ? 1u : 0u) << j;
+    const int cnt = __popc(mask);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < L; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off, L);
+      if (r >= off) incl += o;
+    }
+    const int ncand = __shfl_sync(0xffffffffu, incl, L - 1, L);
+    const bool overflow = ncand > kMaxCand;
+    __syncwarp();
+
+    if (valid && !overflow) {
+      int off = incl - cnt;
+      uint32_t m = mask;
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const int col = 4 * (r + L * (j >> 2)) + (j & 3);
+        const float x = sv[col];
+        float val;
+        uint32_t k;
+        if (SCORING == EXF_SIGMOID) {
+          val = exact_sigmoid(x);
+          k = key_of(__fadd_rn(val, brow ? __ldg(brow + col) : 0.0f));
+        } else {
+          val = x;
+          k = key_of(x);
+        }
+        cand[off] = ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)col);
+        cval[off] = val;
+        ++off;
+      }
+    }
+    __syncwarp();
+    if (valid && !overflow) {
+      for (int c = r; c < ncand; c += L) {
+        const unsigned long long pc = cand[c];
+        int rank = 0;
+        for (int o = 0; o < ncand; ++o) rank += (cand[o] > pc) ? 1 : 0;
+        if (rank < K) {
+          sidx[rank] = (int)(0xFFFFFFFFu - (uint32_t)pc);
+          sval[rank] = cval[c];
+        }
+      }
+    } else if (valid) {
+      // Exact k rounds over all E keys, recomputed from the staged logits each round (rare
+      // path: ties or constant rows).  Group-uniform branch; shuffles use the group mask.
+      uint32_t taken = 0;
+      for (int s = 0; s < K; ++s) {
+        unsigned long long best = 0;  // every packed key is nonzero and unique
+        int bj = -1;
+        for (int j = 0; j < 32; ++j) {
+          if ((taken >> j) & 1u) continue;
+          const int col = 4 * (r + L * (j >> 2)) + (j & 3);
+          const float x = sv[col];
+          const uint32_t k =
+              (SCORING == EXF_SIGMOID)
+                  ? key_of(__fadd_rn(exact_sigmoid(x), brow ? __ldg(brow + col) : 0.0f))
+                  : key_of(x);
+          const unsigned long long pk =
+              ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)col);
+          if (pk > best) {
+            best = pk;
+            bj = j;
+          }
+        }
+        const unsigned long long mine = best;
+#pragma unroll
+        for (int off = 1; off < L; off <<= 1) {
+          const unsigned long long o = __shfl_xor_sync(gmask, best, off, L);
+          best = o > best ? o : best;
+        }
+        if (bj >= 0 && mine == best) taken |= 1u << bj;
+        if (r == 0) {
+          const int col = (int)(0xFFFFFFFFu - (uint32_t)best);
+          sidx[s] = col;
+          sval[s] = (SCORING == EXF_SIGMOID) ? exact_sigmoid(sv[col]) : sv[col];
+        }
+      }
+    }
+    __syncwarp();
+
+    // ---- weights: each slot computed once, by lane (slot % L) ---------------------------------
+    if (valid) {
+      for (int s = r; s < K; s += L)
+        swt[s] = (SCORING == EXF_SOFTMAX) ? exact_exp(__fsub_rn(sval[s], sval[0])) : sval[s];
+    }
+    __syncwarp();
+    float norm = 0.0f;
+    bool divide = true;
+    if (SCORING == EXF_SOFTMAX && !p.renormalize) {
+      // normaliser over all experts: per-lane partial sums, combined in lane order
+      const float m = sval[0];
+      float part = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = 4 * (r + L * (j >> 2)) + (j & 3);
+        part = __fadd_rn(part, exact_exp(__fsub_rn(sv[col], m)));
+      }
+#pragma unroll
+      for (int q = 0; q < L; ++q) norm = __fadd_rn(norm, __shfl_sync(0xffffffffu, part, q, L));
+    } else if (SCORING == EXF_SIGMOID && !p.renormalize) {
+      divide = false;
+    } else {
+      for (int s = 0; s < K; ++s) norm = __fadd_rn(norm, swt[s]);
+    }
+    if (valid) {
+      for (int s = r; s < K; s += L) {
+        float x = divide ? __fdiv_rn(swt[s], norm) : swt[s];
+        if (p.scaling != 1.0f) x = __fmul_rn(x, p.scaling);
+        wf[s] = x;
+      }
+    }
+    __syncwarp();
+
+    if (FOLD == kFoldNone) {
+      if (valid) {
+        for (int s = r; s < K; s += L) {
+          p.out_w[gt * K + s] = wf[s];
+          p.out_ids[gt * K + s] = sidx[s];
+        }
+      }
+      __syncwarp();
+      continue;
+    }
+
+    // ---- prefill fold ----------------------------------------------------------------------
+    const float* coeff = p.coeff + layer * E * E;
+    const float* sel = p.sel_loss + layer * E * E;
+    const int* fidx = sidx;
+    const float* fw = wf;
+    if (FOLD == kFoldDsv4) {
+      // stable sort by weight descending: each slot's rank under (weight desc, slot asc)
+      int* oidx = sm.fidx[warp][g];
+      float* ow = sm.fw[warp][g];
+      if (valid) {
+        for (int s = r; s < K; s += L) {
+          const float ws = wf[s];
+          const uint32_t ks = key_of(ws);
+          int pos = 0;
+          for (int q = 0; q < K; ++q) {
+            const uint32_t kq = key_of(wf[q]);
+            pos += (kq > ks || (kq == ks && q < s)) ? 1 : 0;
+          }
+          oidx[pos] = sidx[s];
+          ow[pos] = ws;
+        }
+      }
+      __syncwarp();
+      fidx = oidx;
+      fw = ow;
+    }
+    int* fpos = sm.fpos[warp][g];
+    float* ft = sm.ft[warp][g];
+    float* ff = sm.ff[warp][g];
+    float* acc = sm.acc[warp][g];
+    if (valid) {
+      for (int j = P + r; j < K; j += L) {
+        const int src = fidx[j];
+        const float wj = fw[j];
+        const float* lrow = sel + (int64_t)src * E;
+        int pos = 0;
+        float best = (FOLD == kFoldQwen3) ? __ldg(lrow + fidx[0]) : FLT_MAX;
+        for (int q = (FOLD == kFoldQwen3) ? 1 : 0; q < P; ++q) {
+          const float c = __ldg(lrow + fidx[q]);
+          if (c < best) {
+            best = c;
+            pos = q;
+          }
+        }
+        const int tgt = fidx[pos];
+        const float s_val = __ldg(coeff + (int64_t)src * E + tgt);
+        if (FOLD == kFoldQwen3) {
+          ft[j] = __fmul_rn(wj, best < 1.0e30f ? s_val : 0.0f);
+        } else {
+          float conf = 1.0f;
+          float lost = 0.0f;
+          if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
+            const float cl = __ldg(p.conf_loss + layer * E * E + (int64_t)src * E + tgt);
+            conf = fminf(fmaxf(__fsub_rn(1.0f, cl), 0.0f), 1.0f);
+            lost = __fmul_rn(wj, __fsub_rn(1.0f, conf));
+          }
+          ft[j] = __fmul_rn(__fmul_rn(wj, s_val), conf);
+          ff[j] = lost;
+        }
+        fpos[j] = pos;
+      }
+    }
+    __syncwarp();
+    if (valid) {
+      const bool blend = FOLD == kFoldDsv4 && p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND;
+      float fs = 0.0f;
+      bool spread = false;
+      if (blend) {
+        float fallback = 0.0f, rsum = 0.0f;
+        for (int j = P; j < K; ++j) fallback = __fadd_rn(fallback, ff[j]);
+        for (int q = 0; q < P; ++q) rsum = __fadd_rn(rsum, fw[q]);
+        spread = rsum > 1.0e-20f;
+        if (spread) fs = __fdiv_rn(fallback, rsum);
+      }
+      for (int q = r; q < P; q += L) {
+        const float wq = fw[q];
+        float a = wq;
+        for (int j = P; j < K; ++j) {
+          const int pj = fpos[j];
+          if (FOLD == kFoldQwen3)
+            a = __fadd_rn(a, q == pj ? ft[j] : 0.0f);
+          else if (q == pj)
+            a = __fadd_rn(a, ft[j]);
+        }
+        if (spread) a = __fadd_rn(a, __fmul_rn(wq, fs));
+        acc[q] = a;
+      }
+    }
+    __syncwarp();
+    if (valid) {
+      float scale = 1.0f;
+      if (FOLD == kFoldDsv4 && p.renorm_mode == EXF_RENORM_ROUTER_L2) {
+        float l2 = 0.0f, f2 = 0.0f;
+        for (int s = 0; s < K; ++s) l2 = __fadd_rn(l2, __fmul_rn(wf[s], wf[s]));
+        for (int q = 0; q < P; ++q) f2 = __fadd_rn(f2, __fmul_rn(acc[q], acc[q]));
+        if (f2 > 1.0e-20f) scale = __fsqrt_rn(__fdiv_rn(l2, f2));
+      }
+      for (int q = r; q < P; q += L) {
+        p.out_w[gt * P + q] = (FOLD == kFoldDsv4) ? __fmul_rn(acc[q], scale) : acc[q];
+        p.out_ids[gt * P + q] = fidx[q];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+
+// Fold of precomputed routes, one thread per token, semantics as the fold stage above.
+template <typename WT, typename IT, int VARIANT>
+__global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.tokens) return;
+  const int K = p.top_k;
+  const int P = p.target_k;
+  const int E = p.experts;
+  const WT* wrow = static_cast<const WT*>(p.w) + t * K;
+  const IT* irow = static_cast<const IT*>(p.ids) + t * K;
+  float w[kMaxK];
+  int id[kMaxK];
+#pragma unroll
+  for (int s = 0; s < kMaxK; ++s) {
+    w[s] = (s < K) ? to_f32(wrow[s]) : 0.0f;
+    id[s] = (s < K) ? (int)irow[s] : 0;
+  }
+  // clamped copies for table lookups (out-of-range ids never read outside the tables)
+  auto cl = [E](int e) { return e < 0 ? 0 : (e >= E ? E - 1 : e); };
+  float fw[kMaxK];
+  int fid[kMaxK];
+  if (VARIANT == EXF_DSV4) {
+    // stable sort descending by weight: rank under (weight desc, slot asc)
+#pragma unroll
+    for (int s = 0; s < kMaxK; ++s) {
+      fw[s] = 0.0f;
+      fid[s] = 0;
+    }
+#pragma unroll
+    for (int s = 0; s < kMaxK; ++s) {
+      if (s < K) {
+        const uint32_t ks = key_of(w[s]);
+        int pos = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxK; ++q)
+          if (q < K && ranks_before(key_of(w[q]), q, ks, s)) ++pos;
+#pragma unroll
+        for (int q = 0; q < kMaxK; ++q)
+          if (q == pos) {
+            fw[q] = w[s];
+            fid[q] = id[s];
+          }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int s = 0; s < kMaxK; ++s) {
+      fw[s] = w[s];
+      fid[s] = id[s];
+    }
+  }
+  float acc[kMaxK];
+#pragma unroll
+  for (int q = 0; q < kMaxK; ++q) acc[q] = fw[q];
+  float fallback = 0.0f;
+#pragma unroll
+  for (int j = 1; j < kMaxK; ++j) {
+    if (j < P || j >= K) continue;
+    const int src = cl(fid[j]);
+    const float* lrow = p.sel_loss + (int64_t)src * E;
+    int pos = 0;
+    float best = (VARIANT == EXF_QWEN3) ? __ldg(lrow + cl(fid[0])) : FLT_MAX;
+#pragma unroll
+    for (int q = (VARIANT == EXF_QWEN3) ? 1 : 0; q < kMaxK; ++q)
+      if (q < P) {
+        const float c = __ldg(lrow + cl(fid[q]));
+        if (c < best) {
+          best = c;
+          pos = q;
+        }
+      }
+    int tgt = fid[0];
+#pragma unroll
+    for (int q = 1; q < kMaxK; ++q)
+      if (q == pos) tgt = fid[q];
+    tgt = cl(tgt);
+    const float s_val = __ldg(p.coeff + (int64_t)src * E + tgt);
+    if (VARIANT == EXF_QWEN3) {
+      const float add = __fmul_rn(fw[j], best < 1.0e30f ? s_val : 0.0f);
+#pragma unroll
+      for (int q = 0; q < kMaxK; ++q)
+        if (q < P) acc[q] = __fadd_rn(acc[q], q == pos ? add : 0.0f);
+    } else {
+      float conf = 1.0f;
+      if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
+        const float c = __ldg(p.conf_loss + (int64_t)src * E + tgt);
+        conf = fminf(fmaxf(__fsub_rn(1.0f, c), 0.0f), 1.0f);
+        fallback = __fadd_rn(fallback, __fmul_rn(fw[j], __fsub_rn(1.0f, conf)));
+      }
+      const float add = __fmul_rn(__fmul_rn(fw[j], s_val), conf);
+#pragma unroll
+      for (int q = 0; q < kMaxK; ++q)
+        if (q == pos) acc[q] = __fadd_rn(acc[q], add);
+    }
+  }
+  float scale = 1.0f;
+  if (VARIANT == EXF_DSV4) {
+    if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
+      float rsum = 0.0f;
+#pragma unroll
+      for (int q = 0; q < kMaxK; ++q)
+        if (q < P) rsum = __fadd_rn(rsum, fw[q]);
+      if (rsum > 1.0e-20f) {
+        const float fs = __fdiv_rn(fallback, rsum);
+#pragma unroll
+        for (int q = 0; q < kMaxK; ++q)
+          if (q < P) acc[q] = __fadd_rn(acc[q], __fmul_rn(fw[q], fs));
+      }
+    } else if (p.renorm_mode == EXF_RENORM_ROUTER_L2) {
+      float l2 = 0.0f, f2 = 0.0f;
+#pragma unroll
+      for (int q = 0; q < kMaxK; ++q) {
+        if (q < K) l2 = __fadd_rn(l2, __fmul_rn(w[q], w[q]));
+        if (q < P) f2 = __fadd_rn(f2, __fmul_rn(acc[q], acc[q]));
+      }
+      if (f2 > 1.0e-20f) scale = __fsqrt_rn(__fdiv_rn(l2, f2));
+    }
+  }
+  WT* ow = static_cast<WT*>(p.out_w) + t * P;
+  IT* oi = static_cast<IT*>(p.out_ids) + t * P;
+#pragma unroll
+  for (int q = 0; q < kMaxK; ++q)
+    if (q < P) {
+      ow[q] = from_f32<WT>(VARIANT == EXF_DSV4 ? __fmul_rn(acc[q], scale) : acc[q]);
+      oi[q] = (IT)fid[q];
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host launchers
+template <int E, int SCORING, int FOLD>
+static cudaError_t launch_router_e(const RouterParams& p, cudaStream_t stream) {
+  using S = RouterShape<E>;
+  auto kern = router_kernel<E, SCORING, FOLD>;
+  const int64_t total = (int64_t)p.layers * p.tokens;
+  const int64_t per_block = (int64_t)S::WARPS * S::TPW;
+  int64_t blocks = (total + per_block - 1) / per_block;
+  const int cap = persistent_grid(reinterpret_cast<const void*>(kern), S::WARPS * 32, 0);
+  if (cap > 0 && blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  kern<<<(unsigned)blocks, S::WARPS * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int SCORING, int FOLD>
+static cudaError_t launch_router_s(int experts, const RouterParams& p, cudaStream_t stream) {
+  switch (experts) {
+    case 64: return launch_router_e<64, SCORING, FOLD>(p, stream);
+    case 128: return launch_router_e<128, SCORING, FOLD>(p, stream);
+    case 256: return launch_router_e<256, SCORING, FOLD>(p, stream);
+    case 512: return launch_router_e<512, SCORING, FOLD>(p, stream);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p,
+                          cudaStream_t stream) {
+  if (scoring == EXF_SOFTMAX) {
+    if (fold == kFoldNone) return launch_router_s<EXF_SOFTMAX, kFoldNone>(experts, p, stream);
+    if (fold == kFoldQwen3) return launch_router_s<EXF_SOFTMAX, kFoldQwen3>(experts, p, stream);
+    return launch_router_s<EXF_SOFTMAX, kFoldDsv4>(experts, p, stream);
+  }
+  if (fold == kFoldNone) return launch_router_s<EXF_SIGMOID, kFoldNone>(experts, p, stream);
+  if (fold == kFoldQwen3) return launch_router_s<EXF_SIGMOID, kFoldQwen3>(experts, p, stream);
+  return launch_router_s<EXF_SIGMOID, kFoldDsv4>(experts, p, stream);
+}
+
+template <typename WT, typename IT>
+static cudaError_t launch_fold_t(int variant, const FoldParams& p, cudaStream_t stream) {
+  const unsigned blocks = (unsigned)((p.tokens + 255) / 256);
+  if (variant == EXF_QWEN3)
+    fold_kernel<WT, IT, EXF_QWEN3><<<blocks, 256, 0, stream>>>(p);
+  else
+    fold_kernel<WT, IT, EXF_DSV4><<<blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename WT>
+static cudaError_t launch_fold_w(int id_dtype, int variant, const FoldParams& p,
+                                 cudaStream_t stream) {
+  return id_dtype == EXF_I32 ? launch_fold_t<WT, int32_t>(variant, p, stream)
+                             : launch_fold_t<WT, int64_t>(variant, p, stream);
+}
+
+cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p,
+                        cudaStream_t stream) {
+  switch (w_dtype) {
+    case EXF_F32: return launch_fold_w<float>(id_dtype, variant, p, stream);
+    case EXF_BF16: return launch_fold_w<__nv_bfloat16>(id_dtype, variant, p, stream);
+    default: return launch_fold_w<__half>(id_dtype, variant, p, stream);
+  }
+}
+
+}  // namespace exf

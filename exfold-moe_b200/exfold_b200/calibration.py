@@ -1,0 +1,113 @@
+"""Calibration table preparation and per-device caching.
+
+The transforms consume the tensors the reference's artifact loaders produce; these helpers
+restate those loaders' preparation steps so callers that build tables themselves get the same
+values:
+
+* prepare_qwen3: exfold/qwen3/vllm_patch.py:45-61 (shape and value checks; coeff := 0 where
+  loss >= 1e30; coeff diagonal := 1; loss diagonal := 1e30).
+* prepare_dsv4: exfold/deepseek_v4/vllm_patch.py:82-170 (key fallbacks; EXFOLD_MAX_PROJECTION_LOSS
+  masking of the decode loss; diagonal fixes; norms clamped to float32 eps).
+* DeviceTables: the per-device copy cache of vllm_patch.py:146-157 / 236-260.
+
+Arrays may be numpy arrays or torch tensors; the result has the input's kind.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+
+_SENTINEL = 1.0e30
+
+
+def _t(a) -> torch.Tensor:
+    return a.detach().clone().float() if isinstance(a, torch.Tensor) else torch.from_numpy(
+        np.array(a, dtype=np.float32, copy=True))
+
+
+def _back(t: torch.Tensor, like):
+    return t if isinstance(like, torch.Tensor) else t.numpy()
+
+
+def prepare_qwen3(coeff, loss, norms, *, validate: bool = True):
+    """[layers, E, E] coeff / loss and [layers, E] norms as the Qwen3 artifact loader leaves them."""
+    c, l_, n = _t(coeff), _t(loss), _t(norms)
+    if c.ndim != 3 or c.shape[1] != c.shape[2]:
+        raise ValueError("coeff must have shape [layers, experts, experts]")
+    if l_.shape != c.shape:
+        raise ValueError("loss and coeff must have identical shapes")
+    if n.shape != c.shape[:2]:
+        raise ValueError("expert_norms must have shape [layers, experts]")
+    if validate:
+        if not all(torch.isfinite(x).all() for x in (c, l_, n)):
+            raise ValueError("artifact contains non-finite values")
+        if torch.any(l_ < 0) or torch.any(n <= 0):
+            raise ValueError("loss must be non-negative and expert_norms positive")
+    c = c.masked_fill(l_ >= _SENTINEL, 0.0)
+    c.diagonal(dim1=-2, dim2=-1).fill_(1.0)
+    l_.diagonal(dim1=-2, dim2=-1).fill_(_SENTINEL)
+    return _back(c, coeff), _back(l_, loss), _back(n, norms)
+
+
+def prepare_dsv4(payload: dict):
+    """(prefill_coeff, prefill_loss, prefill_confidence_loss, decode_coeff, decode_loss, norms)
+    from a DeepSeek-V4 calibration payload, as the DeepSeek-V4 loader builds them."""
+
+    def get(*keys):
+        for k in keys:
+            if k in payload and payload[k] is not None:
+                return payload[k]
+        return None
+
+    pc = _t(get("prefill_coeff", "coeff"))
+    pl = _t(get("prefill_selection_loss", "selection_loss", "loss"))
+    conf = get("prefill_confidence_loss")
+    pcl = _t(conf) if conf is not None else pl.clone()
+    dc = _t(get("decode_coeff", "routing_coeff", "coeff"))
+    dl = _t(get("decode_loss", "routing_loss", "loss"))
+    norms_payload = get("decode_norms", "routing_norms", "norms")
+    if pc.ndim != 3 or pc.shape[1] != pc.shape[2]:
+        raise ValueError(f"prefill_coeff must have shape [layers, experts, experts], got {pc.shape}")
+    for name, t in (("prefill_loss", pl), ("prefill_confidence_loss", pcl), ("decode_coeff", dc),
+                    ("decode_loss", dl)):
+        if t.shape != pc.shape:
+            raise ValueError(f"{name} shape {t.shape} does not match {pc.shape}")
+    if norms_payload is None:
+        raise ValueError("Calibration artifact is missing norms")
+    if isinstance(norms_payload, dict):
+        norms = torch.stack([_t(norms_payload[i]) for i in range(pc.shape[0])])
+    else:
+        norms = _t(norms_payload)
+    if norms.shape != pc.shape[:2]:
+        raise ValueError(f"norms must have shape {pc.shape[:2]}, got {norms.shape}")
+    for name, t in (("prefill_coeff", pc), ("prefill_loss", pl), ("prefill_confidence_loss", pcl),
+                    ("decode_coeff", dc), ("decode_loss", dl)):
+        if not torch.isfinite(t).all():
+            raise ValueError(f"Calibration {name} contains non-finite values")
+    max_loss = float(os.environ.get("EXFOLD_MAX_PROJECTION_LOSS", "1e30"))
+    dl.masked_fill_(dl > max_loss, _SENTINEL)
+    pc.diagonal(dim1=-2, dim2=-1).fill_(1.0)
+    pl.diagonal(dim1=-2, dim2=-1).fill_(_SENTINEL)
+    pcl.diagonal(dim1=-2, dim2=-1).fill_(0.0)
+    dc.diagonal(dim1=-2, dim2=-1).fill_(1.0)
+    dl.diagonal(dim1=-2, dim2=-1).fill_(_SENTINEL)
+    norms = norms.clamp_min(torch.finfo(torch.float32).eps).contiguous()
+    return pc, pl, pcl, dc, dl, norms
+
+
+class DeviceTables:
+    """Per-device cache of one layer's tables (copied once per device, then reused)."""
+
+    def __init__(self, *tables: torch.Tensor):
+        self._host = tuple(t.contiguous() for t in tables)
+        self._cache: dict[torch.device, tuple[torch.Tensor, ...]] = {}
+
+    def on(self, device: torch.device) -> tuple[torch.Tensor, ...]:
+        cached = self._cache.get(device)
+        if cached is None:
+            cached = tuple(t.to(device=device, non_blocking=True) for t in self._host)
+            self._cache[device] = cached
+        return cached

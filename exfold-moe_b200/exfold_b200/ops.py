@@ -1,0 +1,247 @@
+"""torch front end of libexfold_b200.so.
+
+Each function allocates its outputs with torch (so CUDA-graph capture uses the graph's memory
+pool), passes raw device pointers to the C ABI and launches on the current CUDA stream.  Nothing
+here synchronises with the host.  Weights are float32 / bfloat16 / float16 and ids int32 /
+int64 natively; other dtypes are converted on the way in and back on the way out.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+_WDT = {torch.float32: L.EXF_F32, torch.bfloat16: L.EXF_BF16, torch.float16: L.EXF_F16}
+_IDT = {torch.int32: L.EXF_I32, torch.int64: L.EXF_I64}
+_SCORING = {"softmax": L.EXF_SOFTMAX, "sigmoid": L.EXF_SIGMOID}
+_VARIANT = {"qwen3": L.EXF_QWEN3, "dsv4": L.EXF_DSV4}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("ExFold B200 ops require CUDA tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("ExFold B200 ops require all tensors on one device")
+    return dev
+
+
+def _f32c(t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    return t.contiguous() if t.dtype == torch.float32 else t.float().contiguous()
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _weights_in(w: torch.Tensor) -> torch.Tensor:
+    return w.contiguous() if w.dtype in _WDT else w.float().contiguous()
+
+
+def _ids_in(ids: torch.Tensor) -> torch.Tensor:
+    return ids.contiguous() if ids.dtype in _IDT else ids.to(torch.int32).contiguous()
+
+
+# ---- router ---------------------------------------------------------------------------------
+def router_topk(logits: torch.Tensor, top_k: int, scoring: str = "softmax",
+                bias: torch.Tensor | None = None, renormalize: bool = True,
+                scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-k routing of [tokens, experts] logits -> (weights fp32, ids int32) [tokens, top_k]."""
+    dev = _require_cuda(logits, bias)
+    x = _aligned(_f32c(logits))
+    tokens, experts = x.shape
+    b = None if bias is None else _aligned(_f32c(bias))
+    w = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
+    ids = torch.empty((tokens, top_k), dtype=torch.int32, device=dev)
+    L.check(L.lib().exf_router_topk(x.data_ptr(), tokens, experts, top_k, _SCORING[scoring],
+                                    _ptr(b), int(renormalize), float(scaling), w.data_ptr(),
+                                    ids.data_ptr(), _stream(dev)))
+    return w, ids
+
+
+def router_fold_prefill(logits: torch.Tensor, top_k: int, target_k: int, coeff: torch.Tensor,
+                        sel_loss: torch.Tensor, *, scoring: str = "softmax",
+                        bias: torch.Tensor | None = None, renormalize: bool = True,
+                        scaling: float = 1.0, variant: str = "qwen3", renorm_mode: int = 0,
+                        conf_loss: torch.Tensor | None = None,
+                        out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                        ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router + prefill fold in one pass.
+
+    logits [tokens, E] with tables [E, E], or [layers, tokens, E] with tables [layers, E, E]
+    (and bias [layers, E]).  Returns (weights fp32, ids int32) [..., tokens, target_k].
+    """
+    dev = _require_cuda(logits, coeff, sel_loss, bias, conf_loss)
+    x = _aligned(_f32c(logits))
+    layers = 1 if x.dim() == 2 else x.shape[0]
+    tokens, experts = x.shape[-2], x.shape[-1]
+    coeff, sel_loss = _f32c(coeff), _f32c(sel_loss)
+    conf_loss = _f32c(conf_loss)
+    b = None if bias is None else _aligned(_f32c(bias))
+    shape = (*x.shape[:-1], target_k)
+    if out is None:
+        w = torch.empty(shape, dtype=torch.float32, device=dev)
+        ids = torch.empty(shape, dtype=torch.int32, device=dev)
+    else:
+        w, ids = out
+    L.check(L.lib().exf_router_fold_prefill(
+        x.data_ptr(), tokens, layers, experts, top_k, _SCORING[scoring], _ptr(b),
+        int(renormalize), float(scaling), target_k, _VARIANT[variant], int(renorm_mode),
+        coeff.data_ptr(), sel_loss.data_ptr(), _ptr(conf_loss), w.data_ptr(), ids.data_ptr(),
+        _stream(dev)))
+    return w, ids
+
+
+# ---- prefill fold of given routes -------------------------------------------------------------
+def fold_prefill(weights: torch.Tensor, ids: torch.Tensor, coeff: torch.Tensor,
+                 sel_loss: torch.Tensor, target_k: int, *, variant: str = "qwen3",
+                 renorm_mode: int = 0, conf_loss: torch.Tensor | None = None,
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(weights, ids, coeff, sel_loss, conf_loss)
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    tokens, top_k = w_in.shape
+    coeff, sel_loss, conf_loss = _f32c(coeff), _f32c(sel_loss), _f32c(conf_loss)
+    ow = torch.empty((tokens, target_k), dtype=w_in.dtype, device=dev)
+    oi = torch.empty((tokens, target_k), dtype=i_in.dtype, device=dev)
+    if tokens > 0:
+        L.check(L.lib().exf_fold_prefill(
+            w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(), _IDT[i_in.dtype], tokens, top_k,
+            target_k, coeff.shape[0], _VARIANT[variant], int(renorm_mode), coeff.data_ptr(),
+            sel_loss.data_ptr(), _ptr(conf_loss), ow.data_ptr(), oi.data_ptr(), _stream(dev)))
+    return ow.to(weights.dtype), oi.to(ids.dtype)
+
+
+# ---- decode ---------------------------------------------------------------------------------
+def decode(weights: torch.Tensor, ids: torch.Tensor, norms: torch.Tensor, coeff: torch.Tensor,
+           loss: torch.Tensor, budget: int, *, variant: str = "qwen3",
+           subset_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Importance, top-`budget` select, target table and apply in one launch."""
+    dev = _require_cuda(weights, ids, norms, coeff, loss)
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    batch, top_k = w_in.shape
+    norms, coeff, loss = _f32c(norms), _f32c(coeff), _f32c(loss)
+    ow, oi = torch.empty_like(w_in), torch.empty_like(i_in)
+    L.check(L.lib().exf_decode(
+        w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(), _IDT[i_in.dtype], batch, top_k,
+        coeff.shape[0], int(budget), _VARIANT[variant], norms.data_ptr(), coeff.data_ptr(),
+        loss.data_ptr(), ow.data_ptr(), oi.data_ptr(), _ptr(subset_out), _stream(dev)))
+    return ow.to(weights.dtype), oi.to(ids.dtype)
+
+
+def decode_importance(weights: torch.Tensor, ids: torch.Tensor, norms: torch.Tensor,
+                      importance: torch.Tensor) -> torch.Tensor:
+    """Add this shard's fixed-point importance into `importance` (int64 [E], caller-zeroed)."""
+    dev = _require_cuda(weights, ids, norms, importance)
+    if importance.dtype != torch.int64 or not importance.is_contiguous():
+        raise ValueError("importance must be a contiguous int64 vector")
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    norms = _f32c(norms)
+    L.check(L.lib().exf_decode_importance(
+        w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(), _IDT[i_in.dtype], w_in.numel(),
+        norms.numel(), norms.data_ptr(), importance.data_ptr(), _stream(dev)))
+    return importance
+
+
+def decode_apply(importance: torch.Tensor, weights: torch.Tensor, ids: torch.Tensor,
+                 coeff: torch.Tensor, loss: torch.Tensor, budget: int, *, variant: str = "qwen3",
+                 subset_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Select / table / apply from an (all-reduced) importance vector."""
+    dev = _require_cuda(importance, weights, ids, coeff, loss)
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    batch, top_k = w_in.shape
+    coeff, loss = _f32c(coeff), _f32c(loss)
+    ow, oi = torch.empty_like(w_in), torch.empty_like(i_in)
+    L.check(L.lib().exf_decode_apply(
+        importance.data_ptr(), w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(),
+        _IDT[i_in.dtype], batch, top_k, coeff.shape[0], int(budget), _VARIANT[variant],
+        coeff.data_ptr(), loss.data_ptr(), ow.data_ptr(), oi.data_ptr(), _ptr(subset_out),
+        _stream(dev)))
+    return ow.to(weights.dtype), oi.to(ids.dtype)
+
+
+def reroute_subset(weights: torch.Tensor, ids: torch.Tensor, subset: torch.Tensor,
+                   coeff: torch.Tensor, loss: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(weights, ids, subset, coeff, loss)
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    batch, top_k = w_in.shape
+    sub = subset.to(torch.int32).contiguous()
+    coeff, loss = _f32c(coeff), _f32c(loss)
+    ow, oi = torch.empty_like(w_in), torch.empty_like(i_in)
+    L.check(L.lib().exf_reroute_subset(
+        w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(), _IDT[i_in.dtype], batch, top_k,
+        coeff.shape[0], sub.data_ptr(), sub.numel(), coeff.data_ptr(), loss.data_ptr(),
+        ow.data_ptr(), oi.data_ptr(), _stream(dev)))
+    return ow.to(weights.dtype), oi.to(ids.dtype)
+
+
+def static_table(norms: torch.Tensor, coeff: torch.Tensor, loss: torch.Tensor,
+                 budget: int) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(norms, coeff, loss)
+    norms, coeff, loss = _f32c(norms), _f32c(coeff), _f32c(loss)
+    experts = norms.numel()
+    target = torch.empty(experts, dtype=torch.int32, device=dev)
+    scale = torch.empty(experts, dtype=torch.float32, device=dev)
+    L.check(L.lib().exf_static_table(norms.data_ptr(), coeff.data_ptr(), loss.data_ptr(), experts,
+                                     int(budget), target.data_ptr(), scale.data_ptr(),
+                                     _stream(dev)))
+    return target, scale
+
+
+def static_remap_(weights: torch.Tensor, ids: torch.Tensor, target: torch.Tensor,
+                  scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """In place: ids = target[ids], weights *= scale[ids] (contiguous natively-typed tensors)."""
+    dev = _require_cuda(weights, ids, target, scale)
+    if weights.dtype not in _WDT or ids.dtype not in _IDT:
+        raise TypeError("static_remap_ needs float32/bfloat16/float16 weights and int32/int64 ids")
+    if not (weights.is_contiguous() and ids.is_contiguous()):
+        raise ValueError("static_remap_ works in place on contiguous tensors")
+    t = target.to(torch.int32).contiguous()
+    s = _f32c(scale)
+    if weights.numel() > 0:
+        L.check(L.lib().exf_static_remap(weights.data_ptr(), _WDT[weights.dtype], ids.data_ptr(),
+                                         _IDT[ids.dtype], weights.numel(), t.numel(), t.data_ptr(),
+                                         s.data_ptr(), _stream(dev)))
+    return weights, ids
+
+
+# ---- moe_align ------------------------------------------------------------------------------
+def moe_align_capacity(numel: int, experts: int, block_size: int, pad_sorted: bool = False) -> int:
+    return int(L.lib().exf_moe_align_capacity(numel, experts, block_size, int(pad_sorted)))
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
+                         pad_sorted_ids: bool = False,
+                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(sorted_token_ids, expert_ids, num_tokens_post_padded) as vLLM's moe_align_block_size."""
+    dev = _require_cuda(topk_ids)
+    ids = _ids_in(topk_ids)
+    numel = ids.numel()
+    cap = moe_align_capacity(numel, num_experts, block_size, pad_sorted_ids)
+    sorted_ids = torch.empty(cap, dtype=torch.int32, device=dev)
+    expert_ids = torch.empty((cap + block_size - 1) // block_size, dtype=torch.int32, device=dev)
+    post = torch.empty(1, dtype=torch.int32, device=dev)
+    ws_bytes = int(L.lib().exf_moe_align_workspace_bytes(numel, num_experts))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    L.check(L.lib().exf_moe_align(ids.data_ptr(), _IDT[ids.dtype], numel, num_experts, block_size,
+                                  cap, sorted_ids.data_ptr(), expert_ids.data_ptr(),
+                                  post.data_ptr(), ws.data_ptr(), ws_bytes, _stream(dev)))
+    return sorted_ids, expert_ids, post

@@ -1,0 +1,160 @@
+/*
+ * exfold_b200.h - C ABI of the B200 (sm_100a) ExFold routing-transform library
+ * (libexfold_b200.so).
+ *
+ * Every entry point takes raw device pointers, sizes and enums, launches its
+ * kernels on `stream` (a cudaStream_t; NULL = the legacy default stream) and
+ * returns EXF_OK or a negative code; exf_last_error() then holds a message
+ * for the calling thread.  No entry point allocates device memory, copies to
+ * the host or synchronises: callers own every output and workspace buffer, so
+ * the calls can be captured in CUDA graphs.  Calibration tables are fp32,
+ * row-major [source][target], `experts` x `experts`.  Routing tensors are
+ * row-major [tokens][top_k].
+ *
+ * Reference interfaces (paths relative to the reference project root):
+ *   exfold/qwen3/kernels.py                    Triton kernels + host wrappers
+ *   exfold/deepseek_v4/csrc/exfold_kernels.cu  CUDA kernels + ATen launchers
+ *   exfold/deepseek_v4/csrc/exfold_ops.cpp     torch.ops.dsv4_exfold schemas
+ *   vLLM fused_topk / fused_topk_bias / moe_align_block_size, called from
+ *   exfold/qwen3/vllm_patch.py:98-109 and exfold/deepseek_v4/vllm_patch.py:175-209
+ */
+#ifndef EXFOLD_B200_H_
+#define EXFOLD_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define EXF_API __attribute__((visibility("default")))
+#else
+#define EXF_API
+#endif
+
+/* Same type as cudaStream_t, declared here so this header needs no CUDA headers. */
+typedef struct CUstream_st* exf_stream_t;
+
+enum exf_status {
+  EXF_OK = 0,
+  EXF_ERR_INVALID = -1,     /* bad argument: shape, size, null pointer, alignment */
+  EXF_ERR_UNSUPPORTED = -2, /* valid request outside the compiled shapes / dtypes */
+  EXF_ERR_CUDA = -3         /* a CUDA runtime call or kernel launch failed */
+};
+
+enum exf_weight_dtype { EXF_F32 = 0, EXF_BF16 = 1, EXF_F16 = 2 };
+enum exf_index_dtype { EXF_I32 = 0, EXF_I64 = 1 };
+enum exf_scoring { EXF_SOFTMAX = 0, EXF_SIGMOID = 1 };
+
+/* Fold / decode semantics:
+ *   EXF_QWEN3: exfold/qwen3/kernels.py (retain the first P slots as given, drop a transfer whose
+ *              minimum loss is >= 1e30; decode subset may hold zero-importance experts)
+ *   EXF_DSV4:  exfold/deepseek_v4/csrc/exfold_kernels.cu (stable sort by weight, argmin below
+ *              FLT_MAX, renorm modes; decode keeps only positive-importance experts) */
+enum exf_variant { EXF_QWEN3 = 0, EXF_DSV4 = 1 };
+/* EXF_DSV4 prefill renorm_mode (exfold_kernels.cu:94-110) */
+enum exf_renorm { EXF_RENORM_NONE = 0, EXF_RENORM_ROUTER_L2 = 1, EXF_RENORM_SIMILARITY_BLEND = 2 };
+
+EXF_API int exf_abi_version(void);
+EXF_API const char* exf_last_error(void);
+
+/* Router scoring + top-k.  Replaces vLLM fused_topk (softmax; exfold/qwen3/vllm_patch.py:98-109)
+ * and fused_topk_bias (sigmoid + selection bias; exfold/deepseek_v4/vllm_patch.py:175-209).
+ * logits [tokens][experts] fp32, 16-byte aligned; bias [experts] or NULL (sigmoid only).
+ * Slots are ordered by selection key descending, ties by lower expert id.  Weights: softmax
+ * over the selected experts (renormalize) or over all experts; sigmoid of the selected experts,
+ * divided by their sum when renormalize; then times `scaling`.
+ * experts in {32, 64, 128, 256, 512}; 1 <= top_k <= 8. */
+EXF_API int exf_router_topk(const float* logits, int64_t tokens, int experts, int top_k,
+                            int scoring, const float* bias, int renormalize, float scaling,
+                            float* out_w, int32_t* out_ids, exf_stream_t stream);
+
+/* Router + prefill fold in one pass over the logits: the B200 form of the patched prefill router
+ * (exfold/qwen3/vllm_patch.py:166-176 -> kernels.py:97-151; exfold/deepseek_v4/vllm_patch.py:
+ * 262-284 -> exfold_kernels.cu:228-278).  `layers` independent layers are processed in one
+ * launch: logits [layers][tokens][experts], bias [layers][experts], tables
+ * [layers][experts][experts], outputs [layers][tokens][target_k].  conf_loss is used by
+ * EXF_DSV4 with EXF_RENORM_SIMILARITY_BLEND only (may be NULL otherwise). */
+EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int layers, int experts,
+                                    int top_k, int scoring, const float* bias, int renormalize,
+                                    float scaling, int target_k, int variant, int renorm_mode,
+                                    const float* coeff, const float* sel_loss,
+                                    const float* conf_loss, float* out_w, int32_t* out_ids,
+                                    exf_stream_t stream);
+
+/* Prefill fold of precomputed top-k routes.
+ * EXF_QWEN3 replaces project_prefill_topk / _project_prefill_kernel (exfold/qwen3/kernels.py:
+ * 97-151, 9-94); EXF_DSV4 replaces exfold_prefill_cuda / prefill_kernel (exfold/deepseek_v4/
+ * csrc/exfold_kernels.cu:228-278, 17-118).  w [tokens][top_k] (w_dtype), ids [tokens][top_k]
+ * (id_dtype); outputs [tokens][target_k] in the same dtypes.  1 <= target_k <= top_k <= 8
+ * (target_k == top_k folds nothing; EXF_DSV4 still sorts by weight and renormalises). */
+EXF_API int exf_fold_prefill(const void* w, int w_dtype, const void* ids, int id_dtype,
+                             int64_t tokens, int top_k, int target_k, int experts, int variant,
+                             int renorm_mode, const float* coeff, const float* sel_loss,
+                             const float* conf_loss, void* out_w, void* out_ids,
+                             exf_stream_t stream);
+
+/* Decode expert budget in one launch: importance (2^-32 fixed-point, order independent), top-D
+ * select, per-expert target table, apply.
+ * EXF_QWEN3 replaces select_and_reroute_decode (exfold/qwen3/kernels.py:423-491, 4 launches);
+ * EXF_DSV4 replaces exfold_decode_cuda / fused_importance_select_and_apply_kernel
+ * (exfold_kernels.cu:280-322, 120-201).  out_subset [budget] int32 or NULL receives the selected
+ * experts in importance order.  experts <= 1024, 1 <= budget <= experts. */
+EXF_API int exf_decode(const void* w, int w_dtype, const void* ids, int id_dtype, int64_t batch,
+                       int top_k, int experts, int budget, int variant, const float* norms,
+                       const float* coeff, const float* loss, void* out_w, void* out_ids,
+                       int32_t* out_subset, exf_stream_t stream);
+
+/* Split decode for a batch sharded over GPUs: each rank adds its routes' fixed-point importance
+ * into `importance` [experts] int64 (zeroed by the caller), the ranks sum the vectors (one
+ * all-reduce of `experts` int64), then every rank runs exf_decode_apply on its own routes.
+ * Results equal exf_decode on the unsharded batch bit for bit. */
+EXF_API int exf_decode_importance(const void* w, int w_dtype, const void* ids, int id_dtype,
+                                  int64_t routes, int experts, const float* norms,
+                                  int64_t* importance, exf_stream_t stream);
+EXF_API int exf_decode_apply(const int64_t* importance, const void* w, int w_dtype,
+                             const void* ids, int id_dtype, int64_t batch, int top_k,
+                             int experts, int budget, int variant, const float* coeff,
+                             const float* loss, void* out_w, void* out_ids, int32_t* out_subset,
+                             exf_stream_t stream);
+
+/* Reroute to an explicit subset (importance order given by the caller): replaces
+ * reroute_decode_subset / _reroute_decode_kernel (exfold/qwen3/kernels.py:235-292, 154-232).
+ * subset [subset_size] int32 expert ids. */
+EXF_API int exf_reroute_subset(const void* w, int w_dtype, const void* ids, int id_dtype,
+                               int64_t batch, int top_k, int experts, const int32_t* subset,
+                               int subset_size, const float* coeff, const float* loss,
+                               void* out_w, void* out_ids, exf_stream_t stream);
+
+/* Static decode table from calibrated norms: replaces the host-side table build of
+ * exfold/qwen3/vllm_patch.py:130-143.  target [experts] int32, scale [experts] fp32. */
+EXF_API int exf_static_table(const float* norms, const float* coeff, const float* loss,
+                             int experts, int budget, int32_t* target, float* scale,
+                             exf_stream_t stream);
+
+/* In-place static remap ids = target[ids], w = w * scale[ids]: replaces remap_decode_static /
+ * _static_decode_remap_kernel (exfold/qwen3/kernels.py:322-356, 295-319). */
+EXF_API int exf_static_remap(void* w, int w_dtype, void* ids, int id_dtype, int64_t routes,
+                             int experts, const int32_t* target, const float* scale,
+                             exf_stream_t stream);
+
+/* moe_align / permute: replaces vLLM moe_align_block_size (vllm/model_executor/layers/
+ * fused_moe/moe_align_block_size.py:11-93) as used by fused_experts after the ExFold transform.
+ * capacity = exf_moe_align_capacity(); sorted_ids [capacity], expert_ids [ceil(capacity /
+ * block_size)], num_post_pad [1].  Routes of one expert keep ascending flat order; padding
+ * holds `numel`; unused blocks hold expert -1.  `workspace` (exf_moe_align_workspace_bytes
+ * bytes, any contents) may be NULL when that size is 0. */
+EXF_API int64_t exf_moe_align_capacity(int64_t numel, int experts, int block_size,
+                                       int pad_sorted);
+EXF_API int64_t exf_moe_align_workspace_bytes(int64_t numel, int experts);
+EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int experts,
+                          int block_size, int64_t capacity, int32_t* sorted_ids,
+                          int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
+                          int64_t workspace_bytes, exf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXFOLD_B200_H_ */

@@ -56,12 +56,12 @@ ORC_API float orc_sigmoid(float x) {
   return 1.0f / (1.0f + e);
 }
 
-/* Total order on float keys: -0 equals +0, every NaN is one value above +inf. */
+/* Total order on float keys: IEEE 754 totalOrder (a NaN ranks by its sign bit: above +inf
+ * when clear, below -inf when set), except that -0 ranks equal to +0. */
 ORC_API uint32_t orc_key(float x) {
-  uint32_t b = f2u(x);
-  if (x != x) b = 0x7FC00000u;
-  if (b == 0x80000000u) b = 0u;
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  const uint32_t b = f2u(x);
+  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return k == 0x7FFFFFFFu ? 0x80000000u : k;
 }
 
 /* (key desc, index asc): is (ka, ia) ranked before (kb, ib)? */
@@ -300,7 +300,7 @@ ORC_API void orc_reroute_qwen3(const float* w, const int32_t* ids, int64_t route
   }
   for (int64_t r = 0; r < routes; ++r) {
     const int e = ids[r];
-    if (in_subset[e]) {
+    if (e < 0 || e >= experts || in_subset[e]) { /* out-of-range ids pass through */
       out_w[r] = w[r];
       out_ids[r] = e;
     } else {
@@ -370,6 +370,11 @@ ORC_API void orc_decode_dsv4(const float* w, const int32_t* ids, int64_t batch, 
   }
   for (int64_t r = 0; r < routes; ++r) {
     const int e = ids[r];
+    if (e < 0 || e >= experts) { /* out-of-range ids pass through */
+      out_ids[r] = e;
+      out_w[r] = w[r];
+      continue;
+    }
     out_ids[r] = tgt[e];
     out_w[r] = w[r] * scale[e];
   }
@@ -410,10 +415,11 @@ ORC_API void orc_static_table(const float* norms, const float* coeff, const floa
 
 /* In-place static remap, exfold/qwen3/kernels.py:295-319: ids = target[ids],
  * w = w * scale[ids]. */
-ORC_API void orc_static_remap(float* w, int32_t* ids, int64_t routes, const int32_t* target,
-                              const float* scale) {
+ORC_API void orc_static_remap(float* w, int32_t* ids, int64_t routes, int experts,
+                              const int32_t* target, const float* scale) {
   for (int64_t r = 0; r < routes; ++r) {
     const int e = ids[r];
+    if (e < 0 || e >= experts) continue; /* out-of-range ids are left alone */
     w[r] = w[r] * scale[e];
     ids[r] = target[e];
   }

@@ -49,7 +49,7 @@ def _load() -> ctypes.CDLL:
         "orc_decode_dsv4": (None, [_f32p, _i32p, _c.c_int64, _c.c_int, _f32p, _f32p, _f32p,
                                    _c.c_int, _c.c_int, _f32p, _i32p]),
         "orc_static_table": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_int, _i32p, _f32p]),
-        "orc_static_remap": (None, [_f32p, _i32p, _c.c_int64, _i32p, _f32p]),
+        "orc_static_remap": (None, [_f32p, _i32p, _c.c_int64, _c.c_int, _i32p, _f32p]),
         "orc_moe_align_capacity": (_c.c_int64, [_c.c_int64, _c.c_int, _c.c_int, _c.c_int]),
         "orc_moe_align": (None, [_i32p, _c.c_int64, _c.c_int, _c.c_int, _c.c_int64, _i32p, _i32p,
                                  _i32p]),
@@ -169,7 +169,8 @@ def static_table(norms, coeff, loss, budget: int):
 
 def static_remap(w, ids, target, scale):
     w, ids = _f32(w).copy(), _i32(ids).copy()
-    lib().orc_static_remap(w.reshape(-1), ids.reshape(-1), w.size, _i32(target), _f32(scale))
+    lib().orc_static_remap(w.reshape(-1), ids.reshape(-1), w.size, _i32(target).size, _i32(target),
+                           _f32(scale))
     return w, ids
 
 

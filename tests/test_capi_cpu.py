@@ -1,0 +1,106 @@
+"""CPU checks of the C ABI: the library loads without a GPU, exports every symbol the header
+declares, and rejects bad arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from exfold_b200 import _lib as L
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "exfold_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"EXF_API\s+[\w\s\*]+?\b(exf_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_header_symbols():
+    lib = L.lib()
+    names = declared_symbols()
+    assert len(names) >= 14
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in L.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(L.SIGNATURES) == set(names)
+    assert lib.exf_abi_version() == 1
+
+
+def test_capacity_matches_vllm_rule():
+    lib = L.lib()
+    assert lib.exf_moe_align_capacity(12, 5, 4, 0) == 12 + 5 * 3
+    assert lib.exf_moe_align_capacity(12, 5, 4, 1) == 28
+    assert lib.exf_moe_align_capacity(3, 128, 16, 0) == 48  # numel < experts
+    assert lib.exf_moe_align_workspace_bytes(1000, 128) == 0
+    assert lib.exf_moe_align_workspace_bytes(196608, 256) == 96 * 256 * 4
+
+
+def call(name, *args):
+    return getattr(L.lib(), name)(*args)
+
+
+def last_error() -> str:
+    return L.lib().exf_last_error().decode()
+
+
+def test_argument_validation_without_gpu():
+    fake = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    rc = call("exf_router_topk", fake, 10, 96, 8, 0, None, 1, 1.0, fake, fake, None)
+    assert rc == L.EXF_ERR_UNSUPPORTED and "experts" in last_error()
+    rc = call("exf_router_topk", fake, 10, 128, 9, 0, None, 1, 1.0, fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "top_k" in last_error()
+    rc = call("exf_router_topk", ctypes.c_void_p(20), 10, 128, 8, 0, None, 1, 1.0, fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "aligned" in last_error()
+    rc = call("exf_router_fold_prefill", fake, 10, 1, 128, 8, 0, None, 1, 1.0, 9, 0, 0, fake, fake,
+              None, fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "target_k" in last_error()
+    rc = call("exf_router_fold_prefill", fake, 10, 1, 128, 8, 0, None, 1, 1.0, 4, 0, 2, fake, fake,
+              None, fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "renorm_mode" in last_error()
+    rc = call("exf_fold_prefill", fake, 7, fake, 0, 10, 8, 4, 128, 0, 0, fake, fake, None, fake,
+              fake, None)
+    assert rc == L.EXF_ERR_INVALID and "dtype" in last_error()
+    rc = call("exf_decode", fake, 0, fake, 0, 4, 8, 128, 0, 0, fake, fake, fake, fake, fake, None,
+              None)
+    assert rc == L.EXF_ERR_INVALID and "budget" in last_error()
+    rc = call("exf_decode", fake, 0, fake, 0, 4, 8, 2048, 64, 0, fake, fake, fake, fake, fake,
+              None, None)
+    assert rc == L.EXF_ERR_INVALID
+    rc = call("exf_reroute_subset", fake, 0, fake, 0, 4, 8, 128, fake, 0, fake, fake, fake, fake,
+              None)
+    assert rc == L.EXF_ERR_INVALID and "subset_size" in last_error()
+    rc = call("exf_moe_align", fake, 0, 300000, 128, 64, 10, fake, fake, fake, None, 0, None)
+    assert rc == L.EXF_ERR_INVALID and "capacity" in last_error()
+    cap = L.lib().exf_moe_align_capacity(300000, 128, 64, 0)
+    rc = call("exf_moe_align", fake, 0, 300000, 128, 64, cap, fake, fake, fake, None, 0, None)
+    assert rc == L.EXF_ERR_INVALID and "workspace" in last_error()
+    rc = call("exf_moe_align", fake, 0, 100, 2048, 64, 10 ** 6, fake, fake, fake, None, 0, None)
+    assert rc == L.EXF_ERR_UNSUPPORTED
+
+
+def test_empty_inputs_are_no_ops_without_gpu():
+    # zero tokens returns before any CUDA call
+    assert call("exf_router_topk", None, 0, 128, 8, 0, None, 1, 1.0, None, None, None) == 0
+    assert call("exf_fold_prefill", None, 0, None, 0, 0, 8, 4, 128, 0, 0, None, None, None, None,
+                None, None) == 0
+
+
+def test_python_errors_follow_the_reference():
+    import torch
+
+    from exfold_b200.qwen3.kernels import project_prefill_topk, select_and_reroute_decode
+
+    w = torch.rand(4, 8)
+    ids = torch.randint(0, 16, (4, 8))
+    c = torch.rand(16, 16)
+    with pytest.raises(ValueError):
+        project_prefill_topk(w, ids[:, :3], c, 4, c)
+    with pytest.raises(RuntimeError):
+        project_prefill_topk(w, ids, c, 4, c)  # CPU tensors
+    with pytest.raises(ValueError):
+        select_and_reroute_decode(w, ids, torch.rand(16, 2), c, c, 4)

@@ -1,0 +1,205 @@
+"""GPU parity: decode budget (Qwen3 and DeepSeek-V4 semantics), reroute, static remap/table,
+split (sharded) decode, CUDA-graph capture."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from exfold_b200 import ops
+from exfold_b200 import workloads as W
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DEV = torch.device("cuda:0")
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def host(t):
+    torch.cuda.synchronize(DEV)
+    return t.cpu().numpy()
+
+
+def dsv4_tables(lay):
+    coeff, loss = lay.coeff.copy(), lay.loss.copy()
+    np.fill_diagonal(coeff, 1.0)
+    np.fill_diagonal(loss, 1e30)
+    return coeff, loss
+
+
+def test_qwen3_reference_fixtures():
+    from exfold_b200.qwen3.kernels import (remap_decode_static, reroute_decode_subset,
+                                           select_and_reroute_decode)
+
+    qt = np.load(GOLDEN / "qwen3_reference_tests.npz")
+    ow, oi = reroute_decode_subset(cuda(qt["decode_w"]), cuda(qt["decode_ids"]),
+                                   cuda(qt["decode_subset"]), cuda(qt["decode_coeff"]),
+                                   cuda(qt["decode_loss"]))
+    np.testing.assert_array_equal(host(oi), qt["decode_out_ids"])
+    np.testing.assert_array_equal(host(ow), qt["decode_out_w"])
+    w8 = cuda(np.full((1, 8), 0.125, np.float32))
+    i8 = cuda(np.arange(8, dtype=np.int32)[None])
+    dw, di = reroute_decode_subset(w8, i8, i8[0, :4], cuda(np.ones((8, 8), np.float32)),
+                                   cuda(np.full((8, 8), 1e30, np.float32)))
+    np.testing.assert_array_equal(host(dw), qt["noop_decode_w"])
+    np.testing.assert_array_equal(host(di), qt["noop_decode_ids"])
+    ow, oi = select_and_reroute_decode(cuda(qt["select_w"]), cuda(qt["select_ids"]),
+                                       cuda(qt["select_norms"]), cuda(qt["select_coeff"]),
+                                       cuda(qt["select_loss"]), 32)
+    np.testing.assert_array_equal(host(oi), qt["select_out_ids"])
+    np.testing.assert_allclose(host(ow), qt["select_out_w"], atol=5e-5, rtol=5e-5)
+    sw, si = remap_decode_static(cuda(qt["static_w"]), cuda(qt["static_ids"]),
+                                 cuda(qt["static_target"]), cuda(qt["static_scale"]))
+    np.testing.assert_array_equal(host(si), qt["static_out_ids"])
+    np.testing.assert_array_equal(host(sw), qt["static_out_w"])
+
+
+def test_qwen3_decode_workload_config1():
+    wc = np.load(GOLDEN / "workload_cases.npz")
+    lay = W.layer("qwen3_decode")
+    rw, ri = O.router_topk(lay.logits, 8, "softmax")
+    subset = torch.empty(64, dtype=torch.int32, device=DEV)
+    ow, oi = ops.decode(cuda(rw), cuda(ri), cuda(lay.norms), cuda(lay.coeff), cuda(lay.loss), 64,
+                        variant="qwen3", subset_out=subset)
+    ew, ei, es = O.decode_qwen3(rw, ri, lay.norms, lay.coeff, lay.loss, 64)
+    np.testing.assert_array_equal(host(subset), es)
+    np.testing.assert_array_equal(host(oi), ei)
+    np.testing.assert_array_equal(host(ow), ew)
+    np.testing.assert_array_equal(host(subset), wc["qd_subset"])
+    np.testing.assert_array_equal(host(oi), wc["qd_out_ids"])
+    np.testing.assert_allclose(host(ow), wc["qd_out_w"], rtol=1e-5, atol=0)
+
+
+def test_dsv4_reference_fixture_and_graph():
+    from exfold_b200.deepseek_v4.cuda_ops import fold_decode
+
+    dt = np.load(GOLDEN / "dsv4_reference_tests.npz")
+    w = torch.from_numpy(dt["w_bf16_as_f32"]).to(torch.bfloat16).to(DEV)
+    ids = cuda(dt["ids"])
+    ow, oi = fold_decode(w, ids, cuda(dt["coeff"]), cuda(dt["sel"]), cuda(dt["norms"]), 64)
+    np.testing.assert_array_equal(host(oi), dt["decode_out_ids"])
+    np.testing.assert_allclose(host(ow.float()), dt["decode_out_w"], atol=2e-2, rtol=2e-2)
+    ew, ei = O.decode_dsv4(dt["w_bf16_as_f32"], dt["ids"], dt["norms"], dt["coeff"], dt["sel"], 64)
+    np.testing.assert_array_equal(host(oi), ei)
+    np.testing.assert_array_equal(host(ow.float()),
+                                  torch.from_numpy(ew).to(torch.bfloat16).float().numpy())
+    # CUDA graph capture + replay (tests/test_deepseek_v4_cuda.py:96-116), replay == eager
+    coeff, sel, norms = cuda(dt["coeff"]), cuda(dt["sel"]), cuda(dt["norms"])
+    for _ in range(3):
+        fold_decode(w, ids, coeff, sel, norms, 64)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gw, gi = fold_decode(w, ids, coeff, sel, norms, 64)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert gw.shape == w.shape and gi.shape == ids.shape
+    np.testing.assert_array_equal(host(gi), host(oi))
+    np.testing.assert_array_equal(host(gw.float()), host(ow.float()))
+
+
+def test_dsv4_decode_sweep_config3():
+    from exfold_b200.deepseek_v4.cuda_ops import fold_decode
+
+    wc = np.load(GOLDEN / "workload_cases.npz")
+    cfg = W.WORKLOADS["dsv4_decode"]
+    for b in cfg["batches"]:
+        lay = W.Layer(seed=cfg["seed"], tokens=b, experts=256, top_k=8, kind="dsv4")
+        rw, ri = O.router_topk(lay.logits, 8, "sigmoid", lay.bias)
+        coeff, loss = dsv4_tables(lay)
+        for d in cfg["budgets"]:
+            ow, oi = fold_decode(cuda(rw), cuda(ri), cuda(coeff), cuda(loss), cuda(lay.norms), d)
+            ew, ei = O.decode_dsv4(rw, ri, lay.norms, coeff, loss, d)
+            np.testing.assert_array_equal(host(oi), ei)
+            np.testing.assert_array_equal(host(ow), ew)
+            np.testing.assert_array_equal(host(oi), wc[f"dd_b{b}_d{d}_out_ids"])
+            np.testing.assert_allclose(host(ow), wc[f"dd_b{b}_d{d}_out_w"], rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("variant", ["qwen3", "dsv4"])
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("idtype", [torch.int32, torch.int64])
+def test_decode_dtypes_and_sizes(variant, wdtype, idtype):
+    for experts, batch, budget in ((128, 256, 64), (256, 1024, 128), (64, 3, 7), (512, 100, 500)):
+        lay = W.Layer(seed=900 + batch, tokens=batch, experts=experts, top_k=8, kind="qwen3")
+        rw, ri = O.router_topk(lay.logits, 8, "softmax")
+        w_t = torch.from_numpy(rw).to(wdtype)
+        w_in = w_t.float().numpy()
+        ow, oi = ops.decode(w_t.to(DEV), cuda(ri).to(idtype), cuda(lay.norms), cuda(lay.coeff),
+                            cuda(lay.loss), budget, variant=variant)
+        if variant == "qwen3":
+            # exfold/qwen3/kernels.py casts the scale to the weight dtype before multiplying,
+            # so half-precision results may differ from the fp32 oracle by one unit in the last place
+            ew, ei, _ = O.decode_qwen3(w_in, ri, lay.norms, lay.coeff, lay.loss, budget)
+        else:
+            ew, ei = O.decode_dsv4(w_in, ri, lay.norms, lay.coeff, lay.loss, budget)
+        np.testing.assert_array_equal(host(oi).astype(np.int32), ei)
+        got = host(ow.float())
+        ref = torch.from_numpy(ew).to(wdtype).float().numpy()
+        if wdtype == torch.float32:
+            np.testing.assert_array_equal(got, ref)
+        else:
+            np.testing.assert_allclose(got, ref, rtol=2 ** -7, atol=0)
+
+
+def test_split_decode_equals_fused():
+    """importance on shards + summed vector + apply == one fused decode (bit for bit)."""
+    lay = W.layer("qwen3_layers", tokens=1024, layer_index=3)
+    rw, ri = O.router_topk(lay.logits, 8, "softmax")
+    for variant in ("qwen3", "dsv4"):
+        fw, fi = ops.decode(cuda(rw), cuda(ri), cuda(lay.norms), cuda(lay.coeff), cuda(lay.loss),
+                            64, variant=variant)
+        imp = torch.zeros(128, dtype=torch.int64, device=DEV)
+        for shard in np.array_split(np.arange(1024), 4):
+            ops.decode_importance(cuda(rw[shard]), cuda(ri[shard]), cuda(lay.norms), imp)
+        np.testing.assert_array_equal(host(imp), O.importance(rw, ri, lay.norms))
+        outs = [ops.decode_apply(imp, cuda(rw[s]), cuda(ri[s]), cuda(lay.coeff), cuda(lay.loss),
+                                 64, variant=variant) for s in np.array_split(np.arange(1024), 4)]
+        np.testing.assert_array_equal(np.concatenate([host(o[1]) for o in outs]), host(fi))
+        np.testing.assert_array_equal(np.concatenate([host(o[0]) for o in outs]), host(fw))
+
+
+def test_static_table_artifact_layers():
+    art = np.load(GOLDEN / "qwen3_artifact_layers.npz")
+    for layer in (0, 47):
+        p = f"l{layer}_"
+        t, s = ops.static_table(cuda(art[p + "norms"]), cuda(art[p + "coeff"]),
+                                cuda(art[p + "loss"]), 32)
+        np.testing.assert_array_equal(host(t), art[p + "static_target"])
+        np.testing.assert_array_equal(host(s), art[p + "static_scale"])
+        rw, ri = O.router_topk(art[p + "logits"], 8, "softmax")
+        dw, di = ops.decode(cuda(rw[:64]), cuda(ri[:64]), cuda(art[p + "norms"]),
+                            cuda(art[p + "coeff"]), cuda(art[p + "loss"]), 64, variant="qwen3")
+        np.testing.assert_array_equal(host(di), art[p + "decode_out_ids"])
+        np.testing.assert_allclose(host(dw), art[p + "decode_out_w"], rtol=2e-6, atol=1e-8)
+
+
+def test_decode_edge_cases():
+    from exfold_b200.qwen3.kernels import select_and_reroute_decode
+
+    lay = W.layer("qwen3_decode", tokens=16)
+    rw, ri = O.router_topk(lay.logits, 8, "softmax")
+    # budget >= experts and empty batch are passthrough (kernels.py:449-450)
+    w, i = select_and_reroute_decode(cuda(rw), cuda(ri), cuda(lay.norms), cuda(lay.coeff),
+                                     cuda(lay.loss), 500)
+    np.testing.assert_array_equal(host(i), ri)
+    w, i = select_and_reroute_decode(cuda(rw[:0]), cuda(ri[:0]), cuda(lay.norms),
+                                     cuda(lay.coeff), cuda(lay.loss), 8)
+    assert w.shape == (0, 8)
+    # budget 1, all-equal importance (ties -> lowest expert id), out-of-range ids stay untouched
+    ri2 = ri.copy()
+    ri2[0, 0] = 1000
+    ow, oi = ops.decode(cuda(np.ones_like(rw)), cuda(ri2), cuda(np.ones(128, np.float32)),
+                        cuda(lay.coeff), cuda(lay.loss), 1, variant="dsv4")
+    got = host(oi)
+    assert got[0, 0] == 1000
+    ew, ei = O.decode_dsv4(np.ones_like(rw), ri2, np.ones(128, np.float32), lay.coeff, lay.loss, 1)
+    np.testing.assert_array_equal(got, ei)
+    np.testing.assert_array_equal(host(ow), ew)
