@@ -108,19 +108,27 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
   float* swt = sm.sw[warp][g];
   float* wf = sm.wf[warp][g];
 
-  for (int64_t base = ((int64_t)blockIdx.x * S::WARPS + warp) * TPW; base < total; base += stride) {
-    const int64_t gt = base + g;
+  // (layer, token) of this group's token, advanced incrementally (no 64-bit division per step)
+  int64_t gt = ((int64_t)blockIdx.x * S::WARPS + warp) * TPW + g;
+  int64_t layer = gt < total ? gt / p.tokens : 0;
+  int64_t tok = gt - layer * p.tokens;
+  // logits of the current token are prefetched one iteration ahead
+  float4 nv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    nv[i] = gt < total ? ld_stream_f4(p.logits + gt * E + 4 * (r + L * i))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int64_t base = gt - g; base < total; base += stride, gt += stride) {
     const bool valid = gt < total;
-    const int64_t layer = valid ? gt / p.tokens : 0;
-    const float* row = p.logits + (valid ? gt : 0) * E;
     const float* brow = (SCORING == EXF_SIGMOID && p.bias) ? p.bias + layer * E : nullptr;
 
-    // ---- load, stage, selection keys (IEEE total order; exact logits or fast sigmoid) -------
+    // ---- stage, selection keys (IEEE total order; exact logits or fast sigmoid) -------------
     uint32_t keys[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int col = 4 * (r + L * i);
-      float4 v = valid ? ld_stream_f4(row + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 v = nv[i];
       *reinterpret_cast<float4*>(sv + col) = v;
       float x[4] = {v.x, v.y, v.z, v.w};
       if (SCORING == EXF_SIGMOID) {
@@ -170,6 +178,21 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
     }
     const int ncand = __shfl_sync(0xffffffffu, incl, L - 1, L);
     const bool overflow = ncand > kMaxCand;
+
+    // prefetch the next token's logits; they land while this token is ranked and folded
+    const int64_t layer_now = layer;
+    {
+      const int64_t ngt = gt + stride;
+      tok += stride;
+      while (tok >= p.tokens && layer < p.layers) {
+        tok -= p.tokens;
+        ++layer;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        nv[i] = ngt < total ? ld_stream_f4(p.logits + ngt * E + 4 * (r + L * i))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     __syncwarp();
 
     if (valid && !overflow) {
@@ -288,8 +311,8 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
     }
 
     // ---- prefill fold ----------------------------------------------------------------------
-    const float* coeff = p.coeff + layer * E * E;
-    const float* sel = p.sel_loss + layer * E * E;
+    const float* coeff = p.coeff + layer_now * E * E;
+    const float* sel = p.sel_loss + layer_now * E * E;
     const int* fidx = sidx;
     const float* fw = wf;
     if (FOLD == kFoldDsv4) {
@@ -318,28 +341,48 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
     float* ff = sm.ff[warp][g];
     float* acc = sm.acc[warp][g];
     if (valid) {
+      const bool blend = FOLD == kFoldDsv4 && p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND;
+      const float* conf_tab = blend ? p.conf_loss + layer_now * E * E : nullptr;
       for (int j = P + r; j < K; j += L) {
         const int src = fidx[j];
         const float wj = fw[j];
         const float* lrow = sel + (int64_t)src * E;
+        const float* crow = coeff + (int64_t)src * E;
+        // every retained candidate's loss, scale (and confidence) in flight at once
+        float lv[kMaxK], cv[kMaxK], qv[kMaxK];
+        int tv[kMaxK];
+#pragma unroll
+        for (int q = 0; q < kMaxK; ++q) {
+          if (q < P) {
+            tv[q] = fidx[q];
+            lv[q] = __ldg(lrow + tv[q]);
+            cv[q] = __ldg(crow + tv[q]);
+            qv[q] = blend ? __ldg(conf_tab + (int64_t)src * E + tv[q]) : 0.0f;
+          }
+        }
         int pos = 0;
-        float best = (FOLD == kFoldQwen3) ? __ldg(lrow + fidx[0]) : FLT_MAX;
-        for (int q = (FOLD == kFoldQwen3) ? 1 : 0; q < P; ++q) {
-          const float c = __ldg(lrow + fidx[q]);
-          if (c < best) {
-            best = c;
+        float best = (FOLD == kFoldQwen3) ? lv[0] : FLT_MAX;
+#pragma unroll
+        for (int q = (FOLD == kFoldQwen3) ? 1 : 0; q < kMaxK; ++q) {
+          if (q < P && lv[q] < best) {
+            best = lv[q];
             pos = q;
           }
         }
-        const int tgt = fidx[pos];
-        const float s_val = __ldg(coeff + (int64_t)src * E + tgt);
+        float s_val = cv[0], cl = qv[0];
+#pragma unroll
+        for (int q = 1; q < kMaxK; ++q) {
+          if (q == pos) {
+            s_val = cv[q];
+            cl = qv[q];
+          }
+        }
         if (FOLD == kFoldQwen3) {
           ft[j] = __fmul_rn(wj, best < 1.0e30f ? s_val : 0.0f);
         } else {
           float conf = 1.0f;
           float lost = 0.0f;
-          if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
-            const float cl = __ldg(p.conf_loss + layer * E * E + (int64_t)src * E + tgt);
+          if (blend) {
             conf = fminf(fmaxf(__fsub_rn(1.0f, cl), 0.0f), 1.0f);
             lost = __fmul_rn(wj, __fsub_rn(1.0f, conf));
           }
