@@ -293,4 +293,38 @@ EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int expe
   return cuda_status(launch_align(id_dtype, p, (cudaStream_t)stream), name);
 }
 
+// moe_align without any device allocation: the chunk-count table lives in the library's fixed
+// scratch array (exf::g_align_static_table) instead of a caller workspace.
+EXF_API int exf_moe_align_noalloc(const void* ids, int id_dtype, int64_t numel, int experts,
+                                  int block_size, int64_t capacity, int32_t* sorted_ids,
+                                  int32_t* expert_ids, int32_t* num_post_pad,
+                                  exf_stream_t stream) {
+  const char* name = "exf_moe_align_noalloc";
+  EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported id dtype", name);
+  EXF_REQUIRE(numel >= 0 && numel < (int64_t)1 << 31, "%s: numel out of range", name);
+  EXF_REQUIRE(block_size >= 1, "%s: block_size must be >= 1", name);
+  if (experts < 1 || experts > align_max_experts())
+    return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
+  EXF_REQUIRE(capacity >= exf_moe_align_capacity(numel, experts, block_size, 0) ||
+                  capacity >= numel * (int64_t)block_size,
+              "%s: capacity too small", name);
+  EXF_REQUIRE(num_post_pad && (capacity == 0 || (sorted_ids && expert_ids)), "%s: null output",
+              name);
+  EXF_REQUIRE(numel == 0 || ids, "%s: null ids", name);
+  const int64_t entries = align_workspace_bytes(numel, experts) / (int64_t)sizeof(int32_t);
+  const int64_t limit = align_static_table_ints();
+  if (entries > limit) {
+    const int64_t max_numel = (limit / experts) * 2048;
+    return fail(EXF_ERR_INVALID,
+                "%s: %lld routes over %d experts need %lld scratch entries but the fixed scratch "
+                "holds %lld; at most %lld routes for %d experts (use exf_moe_align with a "
+                "workspace for larger inputs)",
+                name, (long long)numel, experts, (long long)entries, (long long)limit,
+                (long long)max_numel, experts);
+  }
+  AlignParams p{ids, numel, experts, block_size, capacity, sorted_ids, expert_ids, num_post_pad,
+                nullptr, 0};
+  return cuda_status(launch_align_static(id_dtype, p, (cudaStream_t)stream), name);
+}
+
 }  // extern "C"

@@ -87,5 +87,7 @@ cudaError_t launch_static_remap(int w_dtype, int id_dtype, void* w, void* ids, i
 cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s);
 int64_t align_workspace_bytes(int64_t numel, int experts);
 int align_max_experts();
+int64_t align_static_table_ints();
+cudaError_t launch_align_static(int id_dtype, AlignParams p, cudaStream_t s);
 
 }  // namespace exf

@@ -205,3 +205,51 @@ cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s) {
 }
 
 }  // namespace exf
+
+// ---- fixed scratch for exf_moe_align_noalloc ---------------------------------------------------
+// Some callers cannot allocate device memory when they call moe_align (see exfold_b200.h); for
+// them the [chunks][experts] count table lives in this file-scope array instead of a caller
+// workspace.  1 MiB of int32 entries; every GPU that loads the library holds it until exit.
+// The count kernel writes every entry the scan reads, so no call needs it zeroed.
+#include <mutex>
+
+namespace exf {
+
+constexpr int64_t kAlignStaticTableInts = 262144;
+static __device__ __align__(256) int32_t g_align_static_table[kAlignStaticTableInts];
+
+constexpr int kStaticTableDevices = 64;
+static std::mutex g_static_table_mu;
+static int32_t* g_static_table_addr[kStaticTableDevices] = {};
+
+int64_t align_static_table_ints() { return kAlignStaticTableInts; }
+
+// Device address of the current device's copy of the array.  In host code the symbol names a
+// host-side stand-in, so the address is looked up once per device, with that device current.
+static cudaError_t align_static_table(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kStaticTableDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_static_table_mu);
+  if (g_static_table_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_align_static_table);
+    if (e != cudaSuccess) return e;
+    g_static_table_addr[dev] = static_cast<int32_t*>(addr);
+  }
+  *out = g_static_table_addr[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_align_static(int id_dtype, AlignParams p, cudaStream_t s) {
+  if (align_workspace_bytes(p.numel, p.experts) > 0) {
+    int32_t* table = nullptr;
+    const cudaError_t e = align_static_table(&table);
+    if (e != cudaSuccess) return e;
+    p.table = table;
+  }
+  return launch_align(id_dtype, p, s);
+}
+
+}  // namespace exf

@@ -153,6 +153,32 @@ EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int expe
                           int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
                           int64_t workspace_bytes, exf_stream_t stream);
 
+/* exf_moe_align for callers that cannot allocate device memory at call time.  This entry point
+ * has no counterpart in the reference.
+ *
+ * Who needs it: exf_moe_align wants a caller workspace above 8192 routes.  Some callers have no
+ * way to provide one per call: an inference-engine plugin whose execute step may not allocate,
+ * a host whose device memory all belongs to another runtime's pool, or code that must not call
+ * cudaMalloc/cudaFree because they synchronise the device.  This variant allocates nothing: the
+ * caller passes only the inputs and outputs, and the [chunks][experts] count table lives in a
+ * fixed 1 MiB array inside the library (262144 int32 entries, held on every GPU that loads the
+ * library until the process exits).
+ *
+ * Limit: ceil(numel / 2048) * experts <= 262144, i.e. at most 2048 * floor(262144 / experts)
+ * routes (4,194,304 at 128 experts, 2,097,152 at 256); larger inputs are rejected with
+ * EXF_ERR_INVALID and a message, never truncated.
+ * Set-up: the first call on each device looks up the array's device address (one
+ * cudaGetSymbolAddress with that device current); make that first call before any stream
+ * capture.
+ * Sharing: all calls on a device use the same array and it keeps the last call's contents (each
+ * call rewrites every entry it reads, so nothing needs clearing).  Calls whose kernels overlap on
+ * the GPU (different streams, or concurrent graphs) race on the array; serialise them.
+ * Outputs and errors are those of exf_moe_align. */
+EXF_API int exf_moe_align_noalloc(const void* ids, int id_dtype, int64_t numel, int experts,
+                                  int block_size, int64_t capacity, int32_t* sorted_ids,
+                                  int32_t* expert_ids, int32_t* num_post_pad,
+                                  exf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
