@@ -207,6 +207,58 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---- decode half of the 48-layer workload -----------------------------------------------------
+DECODE_BATCH, DECODE_BUDGET = 1024, 64
+
+
+def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
+    """Decode budget over all layers for a B=1024 batch split over the ranks: per layer one
+    fixed-point importance launch, one int64 all-reduce of E values, one select/apply launch
+    (a single fused launch on one GPU).  Replayed from a CUDA graph; microseconds per layer."""
+    import torch
+    import torch.distributed as dist
+
+    from exfold_b200 import ops, parallel
+
+    start, end = parallel.shard_range(DECODE_BATCH, world, rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7000)
+    logits = torch.randn((LAYERS, DECODE_BATCH, EXPERTS), generator=gen, device=dev)
+    norms = torch.exp(0.5 * torch.randn((LAYERS, EXPERTS), generator=gen, device=dev))
+    w = torch.empty((LAYERS, end - start, TOP_K), device=dev)
+    ids = torch.empty((LAYERS, end - start, TOP_K), dtype=torch.int32, device=dev)
+    for layer in range(LAYERS):
+        lw, li = ops.router_topk(logits[layer, start:end].contiguous(), TOP_K)
+        w[layer].copy_(lw)
+        ids[layer].copy_(li)
+    imp = torch.zeros((LAYERS, EXPERTS), dtype=torch.int64, device=dev)
+
+    def step():
+        for layer in range(LAYERS):
+            if world == 1:
+                ops.decode(w[layer], ids[layer], norms[layer], coeff[layer], loss[layer],
+                           DECODE_BUDGET, variant="qwen3")
+            else:
+                imp[layer].zero_()
+                ops.decode_importance(w[layer], ids[layer], norms[layer], imp[layer])
+                dist.all_reduce(imp[layer])
+                ops.decode_apply(imp[layer], w[layer], ids[layer], coeff[layer], loss[layer],
+                                 DECODE_BUDGET, variant="qwen3")
+
+    step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    steps = max(10, args.steps // 10)
+    ms = timed(graph.replay, steps) / steps
+    del graph
+    return {"workload": "qwen3_layers_decode", "batch": DECODE_BATCH, "batch_per_gpu": end - start,
+            "budget": DECODE_BUDGET, "layers": LAYERS, "us_per_layer": 1e3 * ms / LAYERS,
+            "launches_per_layer": 1 if world == 1 else 3,
+            "collective": None if world == 1 else "all_reduce int64[128] per layer (NCCL)"}
+
+
 # ---- our arm --------------------------------------------------------------------------------
 def run_ours(args) -> None:
     import torch
@@ -317,6 +369,9 @@ def run_ours(args) -> None:
     h2d = LAYERS * TOKENS * EXPERTS * 4
     d2h = LAYERS * TOKENS * KEEP * 8
 
+    with torch.cuda.stream(stream):
+        decode = measure_decode(dev, world, rank, stream, coeff, loss, timed, args)
+
     cpu = None
     if rank == 0 and world == 1:
         sample = logits[0, :8192].cpu().numpy()
@@ -350,6 +405,7 @@ def run_ours(args) -> None:
                     "ms_per_step": ms_e2e},
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     del graph, gb

@@ -341,16 +341,43 @@ ORC_API void orc_decode_qwen3(const float* w, const int32_t* ids, int64_t batch,
  * 1 (166-173); any other expert maps to the retained expert of smallest loss
  * strictly below FLT_MAX, first in importance order on ties, with scale
  * coeff[src][tgt] (174-192); if no loss qualifies it maps to itself. */
+static void dsv4_apply(const int64_t* imp, const float* w, const int32_t* ids, int64_t routes,
+                       const float* coeff, const float* loss, int experts, int budget,
+                       float* out_w, int32_t* out_ids);
+
 ORC_API void orc_decode_dsv4(const float* w, const int32_t* ids, int64_t batch, int top_k,
                              const float* norms, const float* coeff, const float* loss,
                              int experts, int budget, float* out_w, int32_t* out_ids) {
   const int64_t routes = batch * top_k;
   int64_t* imp = (int64_t*)malloc(sizeof(int64_t) * (size_t)experts);
+  orc_importance(w, ids, routes, norms, experts, imp);
+  dsv4_apply(imp, w, ids, routes, coeff, loss, experts, budget, out_w, out_ids);
+  free(imp);
+}
+
+/* Decode from an importance vector summed elsewhere (a batch sharded over ranks): the select,
+ * table and apply steps of orc_decode_qwen3 (variant 0, without its passthrough) or
+ * orc_decode_dsv4 (variant 1) on this rank's routes. */
+ORC_API void orc_decode_apply(const int64_t* imp, const float* w, const int32_t* ids,
+                              int64_t routes, const float* coeff, const float* loss, int experts,
+                              int budget, int variant, float* out_w, int32_t* out_ids) {
+  if (variant == 1) {
+    dsv4_apply(imp, w, ids, routes, coeff, loss, experts, budget, out_w, out_ids);
+    return;
+  }
+  int32_t* order = (int32_t*)malloc(sizeof(int32_t) * (size_t)experts);
+  orc_order(imp, experts, order);
+  orc_reroute_qwen3(w, ids, routes, order, budget, coeff, loss, experts, out_w, out_ids);
+  free(order);
+}
+
+static void dsv4_apply(const int64_t* imp, const float* w, const int32_t* ids, int64_t routes,
+                       const float* coeff, const float* loss, int experts, int budget,
+                       float* out_w, int32_t* out_ids) {
   int32_t* order = (int32_t*)malloc(sizeof(int32_t) * (size_t)experts);
   char* kept = (char*)calloc((size_t)experts, 1);
   int32_t* tgt = (int32_t*)malloc(sizeof(int32_t) * (size_t)experts);
   float* scale = (float*)malloc(sizeof(float) * (size_t)experts);
-  orc_importance(w, ids, routes, norms, experts, imp);
   orc_order(imp, experts, order);
   for (int p = 0; p < budget && p < experts; ++p)
     if (imp[order[p]] > 0) kept[order[p]] = 1;
@@ -378,7 +405,7 @@ ORC_API void orc_decode_dsv4(const float* w, const int32_t* ids, int64_t batch, 
     out_ids[r] = tgt[e];
     out_w[r] = w[r] * scale[e];
   }
-  free(imp); free(order); free(kept); free(tgt); free(scale);
+  free(order); free(kept); free(tgt); free(scale);
 }
 
 /* ------------------------------------------------------------------------- */

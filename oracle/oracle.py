@@ -48,6 +48,8 @@ def _load() -> ctypes.CDLL:
                                      _c.c_int, _f32p, _i32p]),
         "orc_decode_dsv4": (None, [_f32p, _i32p, _c.c_int64, _c.c_int, _f32p, _f32p, _f32p,
                                    _c.c_int, _c.c_int, _f32p, _i32p]),
+        "orc_decode_apply": (None, [_i64p, _f32p, _i32p, _c.c_int64, _f32p, _f32p, _c.c_int,
+                                    _c.c_int, _c.c_int, _f32p, _i32p]),
         "orc_static_table": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_int, _i32p, _f32p]),
         "orc_static_remap": (None, [_f32p, _i32p, _c.c_int64, _c.c_int, _i32p, _f32p]),
         "orc_moe_align_capacity": (_c.c_int64, [_c.c_int64, _c.c_int, _c.c_int, _c.c_int]),
@@ -155,6 +157,17 @@ def decode_dsv4(w, ids, norms, coeff, loss, budget: int):
     oi = np.empty_like(ids)
     lib().orc_decode_dsv4(w, ids, batch, top_k, norms, coeff, loss, coeff.shape[0], budget,
                           ow, oi)
+    return ow, oi
+
+
+def decode_apply(imp, w, ids, coeff, loss, budget: int, variant: str = "qwen3"):
+    """Select / table / apply from a given (e.g. all-reduced) importance vector."""
+    imp = np.ascontiguousarray(imp, dtype=np.int64)
+    w, ids, coeff, loss = _f32(w), _i32(ids), _f32(coeff), _f32(loss)
+    ow = np.empty_like(w)
+    oi = np.empty_like(ids)
+    lib().orc_decode_apply(imp, w, ids, w.size, coeff, loss, coeff.shape[0], budget,
+                           1 if variant == "dsv4" else 0, ow, oi)
     return ow, oi
 
 
