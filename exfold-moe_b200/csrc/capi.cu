@@ -9,6 +9,7 @@
 #include "exf_common.cuh"
 #include "exf_kernels.h"
 #include "exf_launch.h"
+#include "exf_moe.h"
 
 namespace exf {
 
@@ -291,6 +292,36 @@ EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int expe
   AlignParams p{ids, numel, experts, block_size, capacity, sorted_ids, expert_ids, num_post_pad,
                 static_cast<int32_t*>(workspace), 0};
   return cuda_status(launch_align(id_dtype, p, (cudaStream_t)stream), name);
+}
+
+EXF_API int64_t exf_fused_experts_workspace_bytes(int64_t tokens, int top_k, int experts,
+                                                  int hidden, int inter) {
+  if (tokens < 0 || top_k < 1 || experts < 1 || hidden < 1 || inter < 1) return -1;
+  return moe_workspace(tokens, top_k, experts, hidden, inter, nullptr).bytes;
+}
+
+EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t* topk_ids,
+                              int64_t tokens, int top_k, const void* w13, const void* w2,
+                              int experts, int hidden, int inter, void* y, void* workspace,
+                              int64_t workspace_bytes, int32_t* status, exf_stream_t stream) {
+  const char* name = "exf_fused_experts";
+  EXF_REQUIRE(tokens >= 0 && top_k >= 1 && tokens * top_k < ((int64_t)1 << 31),
+              "%s: bad routing shape", name);
+  if (experts < 1 || experts > align_max_experts())
+    return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
+  if (hidden % 256 != 0 || inter % 128 != 0)
+    return fail(EXF_ERR_UNSUPPORTED,
+                "%s: hidden must be a multiple of 256 and intermediate a multiple of 128", name);
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(x && topk_w && topk_ids && w13 && w2 && y && workspace, "%s: null pointer", name);
+  EXF_REQUIRE(aligned16(x) && aligned16(w13) && aligned16(w2) && aligned16(y) &&
+                  aligned16(workspace),
+              "%s: tensors must be 16-byte aligned", name);
+  MoeWorkspace ws = moe_workspace(tokens, top_k, experts, hidden, inter, workspace);
+  EXF_REQUIRE(workspace_bytes >= ws.bytes, "%s: workspace of %lld bytes required", name,
+              (long long)ws.bytes);
+  MoeArgs a{x, topk_w, topk_ids, tokens, top_k, w13, w2, experts, hidden, inter, y, status};
+  return cuda_status(launch_moe_experts(a, ws, (cudaStream_t)stream), name);
 }
 
 // moe_align without any device allocation: the chunk-count table lives in the library's fixed

@@ -1,0 +1,519 @@
+// Grouped SwiGLU expert GEMMs on the 5th-generation tensor cores (sm_100a: tcgen05 + TMA).
+//
+// After moe_align, routes are grouped by expert and padded to 128-row blocks.  Per MoE layer:
+//   gather : xs[m] = x[token(sorted_ids[m])]                      (bf16 rows; padding rows = 0)
+//   GEMM-1 : act[m, n] = silu(xs[m] . W1[e, n]) * (xs[m] . W3[e, n]) for n in a 128-wide tile;
+//            gate and up rows of W13[e] are stacked into one N = 256 MMA so both accumulators
+//            sit side by side in TMEM and the SwiGLU epilogue needs no second pass
+//   GEMM-2 : out[route, h] = w_route * (act[m] . W2[e, h])         (N = 256 tile of H)
+//   combine: y[t, h] = sum over the token's routes of out[route, h] (fixed order: deterministic)
+//
+// Both GEMMs share one mainloop: a CTA owns one 128 x 256 output tile of one expert; warp 0
+// streams 128 x 64 A and 256 x 64 B bf16 tiles with TMA (128-byte swizzle) through a 4-stage
+// mbarrier pipeline; one elected thread of warp 1 issues tcgen05.mma (M = 128, N = 256, K = 16,
+// fp32 accumulation in TMEM) and releases each stage with tcgen05.commit; warps 2-5 read the
+// accumulator with tcgen05.ld and run the epilogue.  The grid runs the N tiles of one M block
+// next to each other, so A tiles and the expert's weight tiles are reused from L2.
+// Every mbarrier wait is bounded: on time-out the CTA records an error in *status, skips the
+// rest of its work, still frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "exf_common.cuh"
+#include "exf_launch.h"
+#include "exf_moe.h"
+
+namespace exf {
+
+constexpr int kBM = 128;              // rows per M block (moe_align block size)
+constexpr int kBN = 256;              // MMA N
+constexpr int kBK = 64;               // bf16 elements per 128-byte swizzled row
+constexpr int kStages = 4;
+constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kGemmThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTmemCols = 256;
+constexpr uint32_t kWaitLimit = 1u << 20;
+
+struct GemmSmem {
+  alignas(1024) uint8_t tiles[kStages][kStageBytes];
+  alignas(8) uint64_t full[kStages];
+  alignas(8) uint64_t empty[kStages];
+  alignas(8) uint64_t acc_full;
+  uint32_t tmem_base;
+  int failed;
+};
+constexpr size_t kGemmSmemBytes = sizeof(GemmSmem) + 1024;  // + alignment slack
+
+// ---- PTX helpers ------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the CTA marked failed) if the phase does not complete in time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* failed) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*failed) return false;
+    if (i > 32) __nanosleep(64);
+  }
+  *failed = 1;
+  return false;
+}
+// Bounded wait used on the way out: no early exit on the failure flag.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if (i > 32) __nanosleep(64);
+  }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(dst)),
+               "r"(cols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
+}
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Shared-memory matrix descriptor: K-major tile with 128-byte rows, 128-byte swizzle; 8-row
+// groups 1024 bytes apart (SBO), leading offset 16 bytes, descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ---- the shared mainloop + per-GEMM epilogue ------------------------------------------------
+enum GemmKind { kGemmSwiGLU = 0, kGemmDown = 1 };
+
+template <int KIND>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    expert_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, const ExpertGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x;
+  const int m_block = blockIdx.y;
+
+  // blocks past the padded route count, or of no expert, have nothing to do
+  const int post = *p.num_post_pad;
+  if (m_block * kBM >= post) return;
+  const int expert = p.expert_ids[m_block];
+  if (expert < 0 || expert >= p.experts) return;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    sm.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* failed = &sm.failed;
+  const int kblocks = p.k / kBK;
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % kStages;
+        if (!mbar_wait(&sm.empty[s], ((kb / kStages) & 1) ^ 1, failed)) break;
+        ++issued;
+        uint8_t* a_dst = sm.tiles[s];
+        uint8_t* b_dst = sm.tiles[s] + kATileBytes;
+        mbar_expect_tx(&sm.full[s], kStageBytes);
+        tma_load_2d(a_dst, &map_a, &sm.full[s], kb * kBK, m_block * kBM);
+        if (KIND == kGemmSwiGLU) {
+          // gate rows [n0, n0+128) and up rows [I + n0, I + n0 + 128) of W13[expert]
+          const int row0 = expert * 2 * p.n_total + n_tile * (kBN / 2);
+          tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, row0);
+          tma_load_2d(b_dst + kBTileBytes / 2, &map_b, &sm.full[s], kb * kBK, row0 + p.n_total);
+        } else {
+          tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, expert * p.n_total + n_tile * kBN);
+        }
+      }
+      if (*failed) {
+        // let this CTA's copies still in flight land before its shared memory is released
+        for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+          mbar_wait_drain(&sm.full[kb % kStages], (kb / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (one thread)
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < kblocks && ok; ++kb) {
+        const int s = kb % kStages;
+        ok = mbar_wait(&sm.full[s], (kb / kStages) & 1, failed);
+        if (!ok) break;
+        fence_after_sync();
+        const uint32_t a_base = smem_addr(sm.tiles[s]);
+        const uint32_t b_base = a_base + kATileBytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          mma_bf16(tmem, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
+                   (kb > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&sm.empty[s]);
+      }
+      mma_commit(&sm.acc_full);
+    }
+  } else {
+    // ---- epilogue: warps 2-5 own TMEM lanes 32*(warp%4) .. +31, one output row per thread
+    const int q = warp & 3;
+    const int row = m_block * kBM + q * 32 + lane;
+    const bool ok = mbar_wait(&sm.acc_full, 0, failed);
+    fence_after_sync();
+    if (ok && !*failed) {
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+      if (KIND == kGemmSwiGLU) {
+        // act[row, n0 + c] = silu(gate) * up; gate in columns [0,128), up in [128,256)
+        __nv_bfloat16* dst = p.act + (int64_t)row * p.n_total + n_tile * (kBN / 2);
+#pragma unroll 1
+        for (int c = 0; c < kBN / 2; c += 32) {
+          float g[32], u[32];
+          tmem_load32(taddr + c, g);
+          tmem_load32(taddr + kBN / 2 + c, u);
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = g[2 * i] / (1.0f + __expf(-g[2 * i])) * u[2 * i];
+            const float a1 = g[2 * i + 1] / (1.0f + __expf(-g[2 * i + 1])) * u[2 * i + 1];
+            packed[i] = pack_bf16(a0, a1);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        }
+      } else {
+        // out[route, n0 + c] = w_route * acc for real routes; padding rows are dropped.  The
+        // TMEM loads are warp-collective, so every lane runs them and only the stores are
+        // predicated.
+        const int route = p.sorted_ids[row];
+        const bool real = route < p.numel;
+        const float wr = real ? p.route_w[route] : 0.0f;
+        __nv_bfloat16* dst = p.out + (int64_t)(real ? route : 0) * p.hidden + n_tile * kBN;
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          float v[32];
+          tmem_load32(taddr + c, v);
+          if (real) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(pack_bf16(v[8 * i] * wr, v[8 * i + 1] * wr),
+                                 pack_bf16(v[8 * i + 2] * wr, v[8 * i + 3] * wr),
+                                 pack_bf16(v[8 * i + 4] * wr, v[8 * i + 5] * wr),
+                                 pack_bf16(v[8 * i + 6] * wr, v[8 * i + 7] * wr));
+          }
+        }
+      }
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    // the accumulator barrier completes once every issued MMA has finished (immediately on the
+    // normal path, where the epilogue already waited for it)
+    if (lane == 0) mbar_wait_drain(&sm.acc_full, 0);
+    __syncwarp();
+    fence_after_sync();
+    tmem_free(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0 && sm.failed && p.status) atomicExch(p.status, 1);
+}
+
+// ---- gather and combine ---------------------------------------------------------------------
+// xs[m] = x[sorted_ids[m] / top_k] for real routes, zero rows for padding (16-byte vectors).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* x,
+                                                          const int32_t* sorted_ids,
+                                                          const int32_t* num_post_pad,
+                                                          int64_t rows, int numel, int top_k,
+                                                          int hidden, __nv_bfloat16* xs) {
+  const int vec = hidden / 8;
+  const int post = *num_post_pad;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * vec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / vec;
+    const int c = (int)(i - m * vec);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (m < post) {
+      const int route = sorted_ids[m];
+      if (route < numel)
+        v = reinterpret_cast<const uint4*>(x + (int64_t)(route / top_k) * hidden)[c];
+    }
+    reinterpret_cast<uint4*>(xs + m * hidden)[c] = v;
+  }
+}
+
+// y[t] = sum_j out[t * top_k + j] in fp32, route order fixed; routes whose expert id is out of
+// range were never placed by moe_align and contribute nothing.
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* out,
+                                                      const int32_t* ids, int experts,
+                                                      int64_t tokens, int top_k, int hidden,
+                                                      __nv_bfloat16* y) {
+  const int vec = hidden / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tokens * vec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / vec;
+    const int c = (int)(i - t * vec);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < top_k; ++j) {
+      const int e = ids[t * top_k + j];
+      if (e < 0 || e >= experts) continue;
+      const uint4 v = reinterpret_cast<const uint4*>(out + (t * top_k + j) * hidden)[c];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16(acc[0], acc[1]);
+    o.y = pack_bf16(acc[2], acc[3]);
+    o.z = pack_bf16(acc[4], acc[5]);
+    o.w = pack_bf16(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(y + t * hidden)[c] = o;
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// The kernels need more than 48 KB of dynamic shared memory: opt in once per device.
+static cudaError_t allow_gemm_smem() {
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
+}
+
+// 2-D bf16 tensor [rows][cols] (row-major, cols contiguous) read in box_rows x 64 tiles.
+static bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                     uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int64_t moe_capacity(int64_t numel, int experts) {
+  int64_t cap = numel + (int64_t)experts * (kBM - 1);
+  cap = (cap + kBM - 1) / kBM * kBM;
+  if (numel < experts && numel * kBM < cap) cap = numel * kBM;
+  return cap;
+}
+
+static int64_t up256(int64_t b) { return (b + 255) / 256 * 256; }
+
+MoeWorkspace moe_workspace(int64_t tokens, int top_k, int experts, int hidden, int inter,
+                           void* base) {
+  MoeWorkspace w{};
+  const int64_t numel = tokens * top_k;
+  const int64_t cap = moe_capacity(numel, experts);
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t o = off;
+    off += up256(bytes);
+    return base ? static_cast<uint8_t*>(base) + o : nullptr;
+  };
+  w.capacity = cap;
+  w.sorted_ids = reinterpret_cast<int32_t*>(take(cap * 4));
+  w.expert_ids = reinterpret_cast<int32_t*>(take((cap / kBM) * 4));
+  w.num_post_pad = reinterpret_cast<int32_t*>(take(4));
+  w.align_bytes = align_workspace_bytes(numel, experts);
+  w.align_ws = take(w.align_bytes > 0 ? w.align_bytes : 4);
+  w.xs = reinterpret_cast<__nv_bfloat16*>(take(cap * hidden * 2));
+  w.act = reinterpret_cast<__nv_bfloat16*>(take(cap * inter * 2));
+  w.out = reinterpret_cast<__nv_bfloat16*>(take(numel * hidden * 2));
+  w.bytes = off;
+  return w;
+}
+
+cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+  const int64_t numel = a.tokens * a.top_k;
+  const int64_t cap = w.capacity;
+  cudaError_t e = allow_gemm_smem();
+  if (e != cudaSuccess) return e;
+  // 1. moe_align with the GEMM's 128-row blocks
+  AlignParams ap{a.topk_ids, numel, a.experts, kBM, cap, w.sorted_ids, w.expert_ids,
+                 w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
+  e = launch_align(0 /*int32*/, ap, s);
+  if (e != cudaSuccess) return e;
+  // 2. gather token rows into route order
+  {
+    const int64_t work = cap * (a.hidden / 8);
+    int64_t blocks = (work + 255) / 256;
+    const int lim = 8 * sm_count();
+    if (lim > 0 && blocks > lim) blocks = lim;
+    gather_rows_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(a.x), w.sorted_ids, w.num_post_pad, cap, (int)numel,
+        a.top_k, a.hidden, w.xs);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  // 3. GEMM-1 + SwiGLU
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, w.xs, cap, a.hidden, kBM) ||
+      !make_map(&mb, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, kBN / 2))
+    return cudaErrorInvalidValue;
+  ExpertGemmParams p{};
+  p.num_post_pad = w.num_post_pad;
+  p.expert_ids = w.expert_ids;
+  p.sorted_ids = w.sorted_ids;
+  p.experts = a.experts;
+  p.numel = (int)numel;
+  p.hidden = a.hidden;
+  p.status = a.status;
+  p.k = a.hidden;
+  p.n_total = a.inter;
+  p.act = w.act;
+  dim3 g1((unsigned)(a.inter / (kBN / 2)), (unsigned)(cap / kBM));
+  expert_gemm_kernel<kGemmSwiGLU><<<g1, kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // 4. GEMM-2, weighted per-route rows
+  if (!make_map(&ma, w.act, cap, a.inter, kBM) ||
+      !make_map(&mb, a.w2, (uint64_t)a.experts * a.hidden, a.inter, kBN))
+    return cudaErrorInvalidValue;
+  p.k = a.inter;
+  p.n_total = a.hidden;
+  p.route_w = a.topk_w;
+  p.out = w.out;
+  dim3 g2((unsigned)(a.hidden / kBN), (unsigned)(cap / kBM));
+  expert_gemm_kernel<kGemmDown><<<g2, kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // 5. combine the routes of each token
+  {
+    const int64_t work = a.tokens * (a.hidden / 8);
+    int64_t blocks = (work + 255) / 256;
+    const int lim = 8 * sm_count();
+    if (lim > 0 && blocks > lim) blocks = lim;
+    combine_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, s>>>(
+        w.out, a.topk_ids, a.experts, a.tokens, a.top_k, a.hidden,
+        static_cast<__nv_bfloat16*>(a.y));
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace exf

@@ -42,6 +42,9 @@ SIGNATURES = {
     "exf_moe_align_workspace_bytes": (_i64, [_i64, _i]),
     "exf_moe_align": (_i, [_vp, _i, _i64, _i, _i, _i64, _vp, _vp, _vp, _vp, _i64, _vp]),
     "exf_moe_align_noalloc": (_i, [_vp, _i, _i64, _i, _i, _i64, _vp, _vp, _vp, _vp]),
+    "exf_fused_experts_workspace_bytes": (_i64, [_i64, _i, _i, _i, _i]),
+    "exf_fused_experts": (_i, [_vp, _vp, _vp, _i64, _i, _vp, _vp, _i, _i, _i, _vp, _vp, _i64, _vp,
+                               _vp]),
 }
 
 _lock = threading.Lock()

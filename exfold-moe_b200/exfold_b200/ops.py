@@ -245,3 +245,34 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
                                   cap, sorted_ids.data_ptr(), expert_ids.data_ptr(),
                                   post.data_ptr(), ws.data_ptr(), ws_bytes, _stream(dev)))
     return sorted_ids, expert_ids, post
+
+
+# ---- grouped SwiGLU experts (tcgen05) ------------------------------------------------------------
+def fused_experts(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
+                  w13: torch.Tensor, w2: torch.Tensor,
+                  status: torch.Tensor | None = None) -> torch.Tensor:
+    """y = sum_j topk_w[:, j] * W2[e] (silu(W1[e] x) * (W3[e] x)), e = topk_ids[:, j].
+
+    x bf16 [T, H]; w13 bf16 [E, 2I, H] (gate rows then up rows); w2 bf16 [E, H, I].  The layout
+    and meaning follow vLLM's fused_experts.  `status` (int32 [1] on the device) is set to 1 if a
+    pipeline wait timed out.
+    """
+    dev = _require_cuda(x, topk_w, topk_ids, w13, w2)
+    if x.dtype != torch.bfloat16 or w13.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16:
+        raise TypeError("fused_experts computes in bf16: x, w13 and w2 must be bfloat16")
+    x, w13, w2 = x.contiguous(), w13.contiguous(), w2.contiguous()
+    tokens, hidden = x.shape
+    experts, two_i, _ = w13.shape
+    inter = two_i // 2
+    top_k = topk_ids.shape[1]
+    ids = topk_ids.to(torch.int32).contiguous()
+    wts = topk_w.float().contiguous()
+    y = torch.empty_like(x)
+    ws_bytes = int(L.lib().exf_fused_experts_workspace_bytes(tokens, top_k, experts, hidden,
+                                                             inter))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    L.check(L.lib().exf_fused_experts(x.data_ptr(), wts.data_ptr(), ids.data_ptr(), tokens, top_k,
+                                      w13.data_ptr(), w2.data_ptr(), experts, hidden, inter,
+                                      y.data_ptr(), ws.data_ptr(), ws_bytes, _ptr(status),
+                                      _stream(dev)))
+    return y

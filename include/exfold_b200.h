@@ -153,6 +153,22 @@ EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int expe
                           int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
                           int64_t workspace_bytes, exf_stream_t stream);
 
+/* Grouped SwiGLU expert layer on the tcgen05 tensor cores: replaces vLLM fused_experts
+ * (vllm/model_executor/layers/fused_moe/fused_moe.py:1587-1630) as called after the ExFold
+ * transform.  y[t] = sum_j w[t,j] * W2[e] (silu(W1[e] x[t]) * (W3[e] x[t])), e = ids[t,j].
+ * x bf16 [tokens][hidden]; topk_w fp32 and topk_ids int32 [tokens][top_k]; w13 bf16
+ * [experts][2*inter][hidden] (rows [0, inter) gate W1, rows [inter, 2*inter) up W3); w2 bf16
+ * [experts][hidden][inter]; y bf16 [tokens][hidden].  The intermediate activation is rounded to
+ * bf16 (as vLLM's intermediate cache).  workspace: exf_fused_experts_workspace_bytes(), 16-byte
+ * aligned.  status: optional device int32, set to 1 if a pipeline wait timed out.
+ * hidden % 256 == 0, inter % 128 == 0, experts <= 512. */
+EXF_API int64_t exf_fused_experts_workspace_bytes(int64_t tokens, int top_k, int experts,
+                                                  int hidden, int inter);
+EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t* topk_ids,
+                              int64_t tokens, int top_k, const void* w13, const void* w2,
+                              int experts, int hidden, int inter, void* y, void* workspace,
+                              int64_t workspace_bytes, int32_t* status, exf_stream_t stream);
+
 /* exf_moe_align for callers that cannot allocate device memory at call time.  This entry point
  * has no counterpart in the reference.
  *
