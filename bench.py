@@ -413,6 +413,125 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---- additional single-GPU workloads (--workload NAME): one JSON line each --------------------
+def _timed_graph(fn, steps: int, warmup: int, dev) -> float:
+    """ms per call of fn, replayed from a CUDA graph, CUDA events on the capture stream."""
+    import torch
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        fn()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / steps
+    del graph
+    return ms
+
+
+def run_extra(args) -> None:
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
+        ROOT / "MEASURED_PEAKS.json").is_file() else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    steps = max(5, min(args.steps, 200))
+    out = {"workload": args.workload}
+    if args.workload in ("moe_dsv4_prefill", "moe_qwen3_decode"):
+        if args.workload == "moe_dsv4_prefill":
+            lay = W.layer("dsv4_prefill")
+            tokens, experts, hidden, inter = lay.tokens, 256, 4096, 2048
+            coeff, loss = lay.coeff.copy(), lay.loss.copy()
+            np.fill_diagonal(coeff, 1.0)
+            np.fill_diagonal(loss, 1e30)
+            conf = loss.copy()
+            np.fill_diagonal(conf, 0.0)
+            w, ids = ops.router_fold_prefill(
+                torch.from_numpy(lay.logits).to(dev), 8, 3, torch.from_numpy(coeff).to(dev),
+                torch.from_numpy(loss).to(dev), scoring="sigmoid",
+                bias=torch.from_numpy(lay.bias).to(dev), variant="dsv4", renorm_mode=2,
+                conf_loss=torch.from_numpy(conf).to(dev))
+        else:
+            lay = W.layer("qwen3_decode")
+            tokens, experts, hidden, inter = lay.tokens, 128, 2048, 768
+            rw, ri = ops.router_topk(torch.from_numpy(lay.logits).to(dev), 8)
+            w, ids = ops.decode(rw, ri, torch.from_numpy(lay.norms).to(dev),
+                                torch.from_numpy(lay.coeff).to(dev),
+                                torch.from_numpy(lay.loss).to(dev), 64, variant="qwen3")
+        x = torch.randn(tokens, hidden, generator=gen, device=dev).to(torch.bfloat16)
+        w13 = torch.empty(experts, 2 * inter, hidden, dtype=torch.bfloat16, device=dev)
+        w2 = torch.empty(experts, hidden, inter, dtype=torch.bfloat16, device=dev)
+        for e in range(experts):  # N(0, 0.02) weights, generated per expert to bound memory
+            w13[e] = (0.02 * torch.randn(2 * inter, hidden, generator=gen, device=dev))
+            w2[e] = (0.02 * torch.randn(hidden, inter, generator=gen, device=dev))
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        ms = _timed_graph(lambda: ops.fused_experts(x, w, ids, w13, w2, status=status), steps,
+                          max(3, args.warmup), dev)
+        numel = ids.numel()
+        active = int(torch.unique(ids).numel())
+        flops = 6.0 * numel * hidden * inter
+        wbytes = active * 3.0 * hidden * inter * 2
+        out.update(tokens=tokens, routes=numel, active_experts=active, hidden=hidden, inter=inter,
+                   ms_per_layer=ms, tflops=flops / ms / 1e9,
+                   tensor_frac_of_measured_peak=flops / ms / 1e9 / peaks["bf16_tflops"],
+                   weight_gbs=wbytes / ms / 1e6,
+                   hbm_frac_of_measured_peak=wbytes / ms / 1e6 / peaks["hbm_gbs"],
+                   status=int(status.item()), launches=7)
+    elif args.workload == "dsv4_prefill_fold":
+        lay = W.layer("dsv4_prefill")
+        coeff, loss = lay.coeff.copy(), lay.loss.copy()
+        np.fill_diagonal(coeff, 1.0)
+        np.fill_diagonal(loss, 1e30)
+        conf = loss.copy()
+        np.fill_diagonal(conf, 0.0)
+        xs = torch.from_numpy(lay.logits).to(dev)
+        c, l_, cf = (torch.from_numpy(a).to(dev) for a in (coeff, loss, conf))
+        b = torch.from_numpy(lay.bias).to(dev)
+        ow = torch.empty((lay.tokens, 3), device=dev)
+        oi = torch.empty((lay.tokens, 3), dtype=torch.int32, device=dev)
+        ms = _timed_graph(lambda: ops.router_fold_prefill(
+            xs, 8, 3, c, l_, scoring="sigmoid", bias=b, variant="dsv4", renorm_mode=2,
+            conf_loss=cf, out=(ow, oi)), steps, max(3, args.warmup), dev)
+        nbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
+        out.update(tokens=lay.tokens, us_per_launch=ms * 1e3, tokens_per_s=lay.tokens / ms * 1e3,
+                   gbs=nbytes / ms / 1e6, hbm_frac_of_measured_peak=nbytes / ms / 1e6 / peaks["hbm_gbs"])
+    elif args.workload == "dsv4_decode":
+        cfg = W.WORKLOADS["dsv4_decode"]
+        rows = []
+        for batch in cfg["batches"]:
+            lay = W.Layer(seed=cfg["seed"], tokens=batch, experts=256, top_k=8, kind="dsv4")
+            coeff, loss = lay.coeff.copy(), lay.loss.copy()
+            np.fill_diagonal(coeff, 1.0)
+            np.fill_diagonal(loss, 1e30)
+            xs = torch.from_numpy(lay.logits).to(dev)
+            b = torch.from_numpy(lay.bias).to(dev)
+            c, l_, n = (torch.from_numpy(a).to(dev) for a in (coeff, loss, lay.norms))
+            for budget in cfg["budgets"]:
+                def step():
+                    rw, ri = ops.router_topk(xs, 8, "sigmoid", b)
+                    ops.decode(rw, ri, n, c, l_, budget, variant="dsv4")
+                ms = _timed_graph(step, steps, max(3, args.warmup), dev)
+                rows.append({"batch": batch, "budget": budget, "us_router_plus_decode": ms * 1e3})
+        out["sweep"] = rows
+    print(json.dumps(out), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -421,12 +540,17 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller cases for profiling")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="smaller cases for profiling")
+    ap.add_argument("--workload", default="qwen3_layers",
+                    choices=["qwen3_layers", "moe_dsv4_prefill", "moe_qwen3_decode",
+                             "dsv4_prefill_fold", "dsv4_decode"])
     args = ap.parse_args()
     set_shape(args.layers, args.tokens)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "qwen3_layers":
+        run_extra(args)
     else:
         run_ours(args)
 
