@@ -455,7 +455,9 @@ def run_extra(args) -> None:
     out = {"workload": args.workload}
     if args.workload in ("moe_dsv4_prefill", "moe_qwen3_decode"):
         if args.workload == "moe_dsv4_prefill":
-            lay = W.layer("dsv4_prefill")
+            # --tokens / --experts shrink the case for profiling (defaults: the full workload)
+            n_tok = args.tokens if args.tokens != TOKENS else None
+            lay = W.layer("dsv4_prefill", tokens=n_tok)
             tokens, experts, hidden, inter = lay.tokens, 256, 4096, 2048
             coeff, loss = lay.coeff.copy(), lay.loss.copy()
             np.fill_diagonal(coeff, 1.0)
@@ -474,6 +476,9 @@ def run_extra(args) -> None:
             w, ids = ops.decode(rw, ri, torch.from_numpy(lay.norms).to(dev),
                                 torch.from_numpy(lay.coeff).to(dev),
                                 torch.from_numpy(lay.loss).to(dev), 64, variant="qwen3")
+        if args.experts and args.experts < experts:  # profiling: fold the routes onto fewer experts
+            ids = (ids % args.experts).to(ids.dtype)
+            experts = args.experts
         x = torch.randn(tokens, hidden, generator=gen, device=dev).to(torch.bfloat16)
         w13 = torch.empty(experts, 2 * inter, hidden, dtype=torch.bfloat16, device=dev)
         w2 = torch.empty(experts, hidden, inter, dtype=torch.bfloat16, device=dev)
@@ -540,6 +545,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller cases for profiling")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="smaller cases for profiling")
+    ap.add_argument("--experts", type=int, default=0, help="fewer experts (profiling cases)")
     ap.add_argument("--workload", default="qwen3_layers",
                     choices=["qwen3_layers", "moe_dsv4_prefill", "moe_qwen3_decode",
                              "dsv4_prefill_fold", "dsv4_decode"])

@@ -438,27 +438,16 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
 
 // ---------------------------------------------------------------------------------------------
 
-// Fold of precomputed routes, one thread per token, semantics as the fold stage above.
-template <typename WT, typename IT, int VARIANT>
-__global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= p.tokens) return;
-  const int K = p.top_k;
-  const int P = p.target_k;
-  const int E = p.experts;
-  const WT* wrow = static_cast<const WT*>(p.w) + t * K;
-  const IT* irow = static_cast<const IT*>(p.ids) + t * K;
-  float w[kMaxK];
-  int id[kMaxK];
-#pragma unroll
-  for (int s = 0; s < kMaxK; ++s) {
-    w[s] = (s < K) ? to_f32(wrow[s]) : 0.0f;
-    id[s] = (s < K) ? (int)irow[s] : 0;
-  }
-  // clamped copies for table lookups (out-of-range ids never read outside the tables)
+// One token's fold, thread-local: w / id are the top_k routes in router order (K <= 8).  Writes
+// the target_k folded weights (renorm applied) and ids.  Every retained candidate's loss, scale and
+// confidence are gathered together so each omitted route costs one round trip to L2.
+template <int VARIANT>
+__device__ __forceinline__ void fold_token(const float (&w)[kMaxK], const int (&id)[kMaxK], int K,
+                                           int P, int E, const float* coeff, const float* sel,
+                                           const float* conf_tab, int renorm_mode,
+                                           float (&out)[kMaxK], int (&fid)[kMaxK]) {
   auto cl = [E](int e) { return e < 0 ? 0 : (e >= E ? E - 1 : e); };
   float fw[kMaxK];
-  int fid[kMaxK];
   if (VARIANT == EXF_DSV4) {
     // stable sort descending by weight: rank under (weight desc, slot asc)
 #pragma unroll
@@ -489,6 +478,7 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
       fid[s] = id[s];
     }
   }
+  const bool blend = VARIANT == EXF_DSV4 && renorm_mode == EXF_RENORM_SIMILARITY_BLEND;
   float acc[kMaxK];
 #pragma unroll
   for (int q = 0; q < kMaxK; ++q) acc[q] = fw[q];
@@ -497,24 +487,34 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
   for (int j = 1; j < kMaxK; ++j) {
     if (j < P || j >= K) continue;
     const int src = cl(fid[j]);
-    const float* lrow = p.sel_loss + (int64_t)src * E;
+    const float* lrow = sel + (int64_t)src * E;
+    const float* crow = coeff + (int64_t)src * E;
+    const float* qrow = blend ? conf_tab + (int64_t)src * E : nullptr;
+    float lv[kMaxK], cv[kMaxK], qv[kMaxK];
+#pragma unroll
+    for (int q = 0; q < kMaxK; ++q) {
+      if (q < P) {
+        const int t = cl(fid[q]);
+        lv[q] = __ldg(lrow + t);
+        cv[q] = __ldg(crow + t);
+        qv[q] = blend ? __ldg(qrow + t) : 0.0f;
+      }
+    }
     int pos = 0;
-    float best = (VARIANT == EXF_QWEN3) ? __ldg(lrow + cl(fid[0])) : FLT_MAX;
+    float best = (VARIANT == EXF_QWEN3) ? lv[0] : FLT_MAX;
 #pragma unroll
     for (int q = (VARIANT == EXF_QWEN3) ? 1 : 0; q < kMaxK; ++q)
-      if (q < P) {
-        const float c = __ldg(lrow + cl(fid[q]));
-        if (c < best) {
-          best = c;
-          pos = q;
-        }
+      if (q < P && lv[q] < best) {
+        best = lv[q];
+        pos = q;
       }
-    int tgt = fid[0];
+    float s_val = cv[0], cl_val = qv[0];
 #pragma unroll
     for (int q = 1; q < kMaxK; ++q)
-      if (q == pos) tgt = fid[q];
-    tgt = cl(tgt);
-    const float s_val = __ldg(p.coeff + (int64_t)src * E + tgt);
+      if (q == pos) {
+        s_val = cv[q];
+        cl_val = qv[q];
+      }
     if (VARIANT == EXF_QWEN3) {
       const float add = __fmul_rn(fw[j], best < 1.0e30f ? s_val : 0.0f);
 #pragma unroll
@@ -522,9 +522,8 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
         if (q < P) acc[q] = __fadd_rn(acc[q], q == pos ? add : 0.0f);
     } else {
       float conf = 1.0f;
-      if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
-        const float c = __ldg(p.conf_loss + (int64_t)src * E + tgt);
-        conf = fminf(fmaxf(__fsub_rn(1.0f, c), 0.0f), 1.0f);
+      if (blend) {
+        conf = fminf(fmaxf(__fsub_rn(1.0f, cl_val), 0.0f), 1.0f);
         fallback = __fadd_rn(fallback, __fmul_rn(fw[j], __fsub_rn(1.0f, conf)));
       }
       const float add = __fmul_rn(__fmul_rn(fw[j], s_val), conf);
@@ -535,7 +534,7 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
   }
   float scale = 1.0f;
   if (VARIANT == EXF_DSV4) {
-    if (p.renorm_mode == EXF_RENORM_SIMILARITY_BLEND) {
+    if (blend) {
       float rsum = 0.0f;
 #pragma unroll
       for (int q = 0; q < kMaxK; ++q)
@@ -546,7 +545,7 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
         for (int q = 0; q < kMaxK; ++q)
           if (q < P) acc[q] = __fadd_rn(acc[q], __fmul_rn(fw[q], fs));
       }
-    } else if (p.renorm_mode == EXF_RENORM_ROUTER_L2) {
+    } else if (renorm_mode == EXF_RENORM_ROUTER_L2) {
       float l2 = 0.0f, f2 = 0.0f;
 #pragma unroll
       for (int q = 0; q < kMaxK; ++q) {
@@ -556,12 +555,36 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
       if (f2 > 1.0e-20f) scale = __fsqrt_rn(__fdiv_rn(l2, f2));
     }
   }
+#pragma unroll
+  for (int q = 0; q < kMaxK; ++q) out[q] = (VARIANT == EXF_DSV4) ? __fmul_rn(acc[q], scale) : acc[q];
+}
+
+// Fold of precomputed routes, one thread per token, semantics as the fold stage above.
+template <typename WT, typename IT, int VARIANT>
+__global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.tokens) return;
+  const int K = p.top_k;
+  const int P = p.target_k;
+  const WT* wrow = static_cast<const WT*>(p.w) + t * K;
+  const IT* irow = static_cast<const IT*>(p.ids) + t * K;
+  float w[kMaxK];
+  int id[kMaxK];
+#pragma unroll
+  for (int s = 0; s < kMaxK; ++s) {
+    w[s] = (s < K) ? to_f32(wrow[s]) : 0.0f;
+    id[s] = (s < K) ? (int)irow[s] : 0;
+  }
+  float out[kMaxK];
+  int fid[kMaxK];
+  fold_token<VARIANT>(w, id, K, P, p.experts, p.coeff, p.sel_loss, p.conf_loss, p.renorm_mode, out,
+                      fid);
   WT* ow = static_cast<WT*>(p.out_w) + t * P;
   IT* oi = static_cast<IT*>(p.out_ids) + t * P;
 #pragma unroll
   for (int q = 0; q < kMaxK; ++q)
     if (q < P) {
-      ow[q] = from_f32<WT>(VARIANT == EXF_DSV4 ? __fmul_rn(acc[q], scale) : acc[q]);
+      ow[q] = from_f32<WT>(out[q]);
       oi[q] = (IT)fid[q];
     }
 }
