@@ -456,8 +456,7 @@ def run_extra(args) -> None:
     if args.workload in ("moe_dsv4_prefill", "moe_qwen3_decode"):
         if args.workload == "moe_dsv4_prefill":
             # --tokens / --experts shrink the case for profiling (defaults: the full workload)
-            n_tok = args.tokens if args.tokens != TOKENS else None
-            lay = W.layer("dsv4_prefill", tokens=n_tok)
+            lay = W.layer("dsv4_prefill", tokens=args.tokens)
             tokens, experts, hidden, inter = lay.tokens, 256, 4096, 2048
             coeff, loss = lay.coeff.copy(), lay.loss.copy()
             np.fill_diagonal(coeff, 1.0)
@@ -544,13 +543,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller cases for profiling")
-    ap.add_argument("--tokens", type=int, default=TOKENS, help="smaller cases for profiling")
+    ap.add_argument("--tokens", type=int, default=None, help="smaller cases for profiling")
     ap.add_argument("--experts", type=int, default=0, help="fewer experts (profiling cases)")
     ap.add_argument("--workload", default="qwen3_layers",
                     choices=["qwen3_layers", "moe_dsv4_prefill", "moe_qwen3_decode",
                              "dsv4_prefill_fold", "dsv4_decode"])
     args = ap.parse_args()
-    set_shape(args.layers, args.tokens)
+    set_shape(args.layers, args.tokens or TOKENS)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
