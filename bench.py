@@ -395,7 +395,7 @@ def run_ours(args) -> None:
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "traffic": profiled_traffic("router_fold_qwen3_layer"),
                          "peak_source": peaks["source"],
-                         "kernel": "exf::router_kernel<128, softmax, qwen3 fold>",
+                         "kernel": "exf::router_tpt_kernel<qwen3 fold, P=4>",
                          "bytes_per_launch": bytes_per_launch(TOKENS),
                          "us_per_launch": launch_s * 1e6},
             "layer_batched": {"ms_per_step": ms_b, "tokens_per_s": tokens_per_step / (ms_b / 1e3),

@@ -74,6 +74,10 @@ struct AlignParams {
 };
 
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p, cudaStream_t s);
+// One token per thread, bulk-copied tiles: 128 experts, softmax, top-8, renormalised, Qwen3 fold
+// or none, 16-byte aligned logits and outputs.
+bool router_tpt_eligible(int experts, int scoring, int fold, const RouterParams& p);
+cudaError_t launch_router_tpt(int fold, const RouterParams& p, cudaStream_t s);
 cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p, cudaStream_t s);
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,

@@ -1,0 +1,500 @@
+// Router top-8 (+ Qwen3 prefill fold) for 128 experts, one token per thread (sm_100a).
+//
+// router_tpt_kernel serves the prefill router of 128-expert softmax models (top-8, renormalised),
+// optionally fused with the ExFold prefill fold (exfold/qwen3/kernels.py:9-94 semantics):
+//   * The logits stream through a ring of 10 tile slots (32 tokens x 512 B each) per CTA, filled
+//     by bulk copies (cp.async.bulk, mbarrier completion) and shared by 8 warps: a warp takes
+//     the next tile of the layer, ranks it, and refills the slot with the tile 10 places ahead
+//     as soon as its selection has read it, publishing the tile index so that the slot's next
+//     reader knows which barrier phase to wait for.  Lane t owns token t of the tile and reads
+//     its row in the chunk order i ^ (t & 7): rows are 512 B apart, so the 8 lanes of each
+//     quarter-warp hit 8 different 16-byte bank quads and the reads are conflict-free.
+//   * Selection keys are IEEE totalOrder keys of the logits.  The 32 groups of 4 consecutive
+//     columns give 32 group maxima; their keys, with the low 5 bits replaced by the group's slot,
+//     go through a sorting network (4 x 19-comparator sorts, 3 merges) whose top 8 name the 8
+//     groups with the largest maxima.  Those groups are reloaded, their exact maxima sorted as
+//     (key desc, column asc), and every other element of those groups that reaches the 8th
+//     maximum is inserted.  When exactly 8 groups reach the 8th maximum and it is positive, this
+//     is the exact top 8 (every element that reaches it lies in those groups; no zeros, so -0 and
+//     +0 cannot tie).  Other tokens (ties of group maxima, zeros among the candidates) insert
+//     every element of every group that reaches the truncated bound instead: exact, slower.
+//   * The fold's loss lookups (4 per omitted route) go to a shared-memory copy of the layer's
+//     128 x 128 loss table, loaded once per CTA and layer: scattered 4-byte reads from L1/L2 cost
+//     one pass per distinct line (32 per warp instruction), shared memory only its bank
+//     conflicts.  The one scale per omitted route is read from L2 while the weights are
+//     computed.  Each CTA ranks a contiguous range of the (layer, tile) sequence, so it loads
+//     one table per layer boundary it crosses.
+#include <float.h>
+
+#include <mutex>
+
+#include "exf_common.cuh"
+#include "exf_kernels.h"
+#include "exf_launch.h"
+
+namespace exf {
+namespace {
+
+constexpr int kE = 128;
+constexpr int kK = 8;
+constexpr int kWarps = 8;                // warps per CTA, each ranking one tile at a time
+constexpr int kSlots = 10;               // tile slots per CTA: a ring shared by its warps
+constexpr int kRows = 32;                // tokens per tile: one per lane
+constexpr int kTileFloats = kRows * kE;  // 16 KB
+constexpr uint32_t kSpinLimit = 1u << 20;
+
+struct TptSmem {
+  float tile[kSlots][kTileFloats];
+  float loss[kE * kE];     // the current layer's selection-loss table (fold only)
+  uint64_t bar[kSlots];    // tile copies
+  uint64_t tbar;           // table copies
+  long long seq[kSlots];   // CTA-local index of the tile whose copy the slot's barrier tracks
+  long long done[kSlots];  // CTA-local index of the last tile whose copy was waited for
+  int next;                // next tile of the current layer to hand out
+  int failed;              // a wait timed out: the remaining tiles are marked, not ranked
+};
+constexpr size_t kTptSmemBytes = sizeof(TptSmem) + 128;  // + alignment slack
+static_assert(kTptSmemBytes <= 232448, "router_tpt: shared memory over the per-CTA limit");
+
+__device__ __forceinline__ uint32_t saddr(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+__device__ __forceinline__ void bar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool bar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(ok)
+      : "r"(saddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for a tile; false if the copy did not complete within the limit.
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (bar_test(bar, parity)) return true;
+    if (i > 16) __nanosleep(32);
+  }
+  return false;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(saddr(dst)),
+      "l"(src), "r"(bytes), "r"(saddr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void cx32(uint32_t& a, uint32_t& b) {
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+__device__ __forceinline__ void cx64(uint64_t& a, uint64_t& b) {
+  const bool swap = a < b;
+  const uint64_t hi = swap ? b : a, lo = swap ? a : b;
+  a = hi;
+  b = lo;
+}
+// Optimal 19-comparator network for 8 inputs, descending.
+template <typename T, void (*CX)(T&, T&)>
+__device__ __forceinline__ void sort8(T* v) {
+  CX(v[0], v[2]); CX(v[1], v[3]); CX(v[4], v[6]); CX(v[5], v[7]);
+  CX(v[0], v[4]); CX(v[1], v[5]); CX(v[2], v[6]); CX(v[3], v[7]);
+  CX(v[0], v[1]); CX(v[2], v[3]); CX(v[4], v[5]); CX(v[6], v[7]);
+  CX(v[2], v[4]); CX(v[3], v[5]);
+  CX(v[1], v[4]); CX(v[3], v[6]);
+  CX(v[1], v[2]); CX(v[3], v[4]); CX(v[5], v[6]);
+}
+// a, b sorted descending -> a = the 8 largest of both, sorted descending.
+__device__ __forceinline__ void merge8(uint32_t* a, const uint32_t* b) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = max(a[i], b[7 - i]);
+  cx32(a[0], a[4]); cx32(a[1], a[5]); cx32(a[2], a[6]); cx32(a[3], a[7]);
+  cx32(a[0], a[2]); cx32(a[1], a[3]); cx32(a[4], a[6]); cx32(a[5], a[7]);
+  cx32(a[0], a[1]); cx32(a[2], a[3]); cx32(a[4], a[5]); cx32(a[6], a[7]);
+}
+// Insert v into T (sorted descending), dropping the smallest.
+__device__ __forceinline__ void insert8(uint64_t (&T)[kK], uint64_t v) {
+#pragma unroll
+  for (int q = 0; q < kK; ++q) cx64(T[q], v);
+}
+__device__ __forceinline__ uint64_t pack(uint32_t key, int col) {
+  return (static_cast<uint64_t>(key) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(col));
+}
+
+template <int FOLD, int P>
+__global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const RouterParams p) {
+  extern __shared__ uint8_t tpt_raw[];
+  TptSmem& sm = *reinterpret_cast<TptSmem*>((reinterpret_cast<uintptr_t>(tpt_raw) + 127) &
+                                            ~static_cast<uintptr_t>(127));
+  const int warp = threadIdx.x >> 5;
+  const int t = threadIdx.x & 31;
+  const int sw = t & 7;
+  const int64_t tokens = p.tokens;
+  // Tiles never straddle a layer (the last one of a layer may be short): global tile g is tile
+  // g % tpl of layer g / tpl.  This CTA ranks the contiguous range [g0, g0 + nk), so it crosses
+  // few layer boundaries; its local tile k is global tile g0 + k.
+  const int64_t tpl = (tokens + kRows - 1) / kRows;
+  const int64_t ntiles = tpl * p.layers;
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * ntiles / gridDim.x;
+  const int64_t nk = (static_cast<int64_t>(blockIdx.x) + 1) * ntiles / gridDim.x - g0;
+  volatile long long* seq = sm.seq;
+  volatile int* failed = &sm.failed;
+
+  auto issue = [&](int64_t k) {  // local tile k into slot k % kSlots
+    const int slot = static_cast<int>(k % kSlots);
+    const int64_t l = (g0 + k) / tpl, tl = (g0 + k) - l * tpl;
+    const int64_t rows = tokens - tl * kRows < kRows ? tokens - tl * kRows : kRows;
+    const uint32_t bytes = static_cast<uint32_t>(rows * kE * sizeof(float));
+    bar_expect(&sm.bar[slot], bytes);
+    bulk_load(sm.tile[slot], p.logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      bar_init(&sm.bar[s]);
+      sm.seq[s] = -1;
+      sm.done[s] = -1;
+    }
+    bar_init(&sm.tbar);
+    sm.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (FOLD != kFoldNone && nk > 0) {  // the first layer's table ahead of the first tiles
+      bar_expect(&sm.tbar, kE * kE * sizeof(float));
+      bulk_load(sm.loss, p.sel_loss + (g0 / tpl) * kE * kE, kE * kE * sizeof(float), &sm.tbar);
+    }
+    for (int s = 0; s < kSlots && s < nk; ++s) {
+      sm.seq[s] = s;
+      issue(s);
+    }
+  }
+  __syncthreads();
+
+  // thread 0: phase (0, 1, ...) of the table copy issued and not yet waited for (-1: none)
+  int64_t table_pending = FOLD != kFoldNone && nk > 0 ? 0 : -1;
+  // layer segments of the range: [ks, ke) of local tiles in layer l, the phase-th segment
+  int phase = 0;
+  for (int64_t ks = 0; ks < nk; ++phase) {
+    const int64_t l = (g0 + ks) / tpl;
+    const int64_t ke = ((l + 1) * tpl - g0) < nk ? (l + 1) * tpl - g0 : nk;
+    const int n = static_cast<int>(ke - ks);
+    // ---- this layer's loss table into shared memory (all reads of the previous one are done)
+    if (threadIdx.x == 0) {
+      sm.next = 0;
+      if (FOLD != kFoldNone && phase > 0 && !*failed) {
+        bar_expect(&sm.tbar, kE * kE * sizeof(float));
+        bulk_load(sm.loss, p.sel_loss + l * kE * kE, kE * kE * sizeof(float), &sm.tbar);
+        table_pending = phase;
+      }
+    }
+    __syncthreads();
+    if (FOLD != kFoldNone) {
+      bool ok = !*failed && bar_wait(&sm.tbar, static_cast<uint32_t>(phase) & 1u);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) *failed = 1;
+      if (threadIdx.x == 0 && ok) table_pending = -1;
+    }
+    const float* coeff = p.coeff + l * kE * kE;
+
+    while (true) {
+      int j = 0;
+      if (t == 0) j = atomicAdd(&sm.next, 1);
+      j = __shfl_sync(0xffffffffu, j, 0);
+      if (j >= n) break;
+      const int64_t k = ks + j;
+      const int slot = static_cast<int>(k % kSlots);
+      // the slot must hold tile k's copy before its barrier parity means anything: the lane that
+      // refills a slot publishes the tile index after issuing the copy
+      bool ok = !*failed;
+      if (ok && t == 0) {
+        uint32_t i = 0;
+        while (seq[slot] != k && !*failed && i < kSpinLimit)
+          if (++i > 16) __nanosleep(32);
+        ok = seq[slot] == k;
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok) ok = bar_wait(&sm.bar[slot], static_cast<uint32_t>(k / kSlots) & 1u);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        if (t == 0) sm.done[slot] = k;
+      } else {
+        *failed = 1;
+      }
+      const int64_t tok = (g0 + k - l * tpl) * kRows + t;
+      const bool valid = tok < tokens;
+      const int64_t row = l * tokens + tok;
+      float* rowp = sm.tile[slot] + t * kE;
+      uint64_t T[kK];
+
+      // ======== phase 1: the selection, the only part that reads the tile =====================
+      if (ok) {
+        // ---- group maxima (slot u = 8 s + i holds columns 32 s + 4 (i ^ sw) .. + 3) ---------
+        uint32_t gmx[32];
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 v = *reinterpret_cast<const float4*>(rowp + 32 * s + 4 * (i ^ sw));
+            gmx[8 * s + i] = max(max(order_key(v.x), order_key(v.y)),
+                                 max(order_key(v.z), order_key(v.w)));
+          }
+        uint32_t pk[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) pk[u] = (gmx[u] & ~31u) | (31u - u);
+        sort8<uint32_t, cx32>(pk);
+        sort8<uint32_t, cx32>(pk + 8);
+        sort8<uint32_t, cx32>(pk + 16);
+        sort8<uint32_t, cx32>(pk + 24);
+        merge8(pk, pk + 8);
+        merge8(pk + 16, pk + 24);
+        merge8(pk, pk + 16);
+
+        // ---- the 8 named groups: exact maxima, sorted by (key desc, column asc) -------------
+        uint32_t ek[kK][4];
+        int cb[kK], emax[kK];
+#pragma unroll
+        for (int i = 0; i < kK; ++i) {
+          const uint32_t u = 31u - (pk[i] & 31u);
+          cb[i] = 32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw);
+          const float4 v = *reinterpret_cast<const float4*>(rowp + cb[i]);
+          ek[i][0] = order_key(v.x);
+          ek[i][1] = order_key(v.y);
+          ek[i][2] = order_key(v.z);
+          ek[i][3] = order_key(v.w);
+          const uint32_t m = max(max(ek[i][0], ek[i][1]), max(ek[i][2], ek[i][3]));
+          emax[i] = ek[i][0] == m ? 0 : (ek[i][1] == m ? 1 : (ek[i][2] == m ? 2 : 3));
+          T[i] = pack(m, cb[i] + emax[i]);
+        }
+        sort8<uint64_t, cx64>(T);
+        const uint32_t theta = static_cast<uint32_t>(T[kK - 1] >> 32);
+        int reach = 0;
+#pragma unroll
+        for (int u = 0; u < 32; ++u) reach += gmx[u] >= theta ? 1 : 0;
+        const bool fast = reach == kK && theta > kKeyPosZero;
+
+        if (fast) {
+          // other elements of the named groups that reach theta, listed in this lane's own row
+          // (its logits are no longer needed); the entry offset by lane keeps bank pairs apart
+          uint64_t* xl = reinterpret_cast<uint64_t*>(rowp);
+          int nx = 0;
+#pragma unroll
+          for (int i = 0; i < kK; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (e != emax[i] && ek[i][e] >= theta) {
+                xl[(t + nx) & 63] = pack(ek[i][e], cb[i] + e);
+                ++nx;
+              }
+          for (int m = 0; m < nx; ++m) insert8(T, xl[(t + m) & 63]);
+        } else if (valid) {
+          // exact insertion over every element of every group whose maximum reaches the bound
+          // (pk[7] truncated is below the 8th largest key; -0 ranks equal to +0)
+          const uint32_t lb = pk[kK - 1] & ~31u;
+          uint32_t gm = 0;
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            const uint32_t gk = gmx[u] == kKeyNegZero ? kKeyPosZero : gmx[u];
+            gm |= (gk >= lb ? 1u : 0u) << u;
+          }
+#pragma unroll
+          for (int q = 0; q < kK; ++q) T[q] = 0;
+          while (gm) {
+            const uint32_t u = static_cast<uint32_t>(__ffs(gm) - 1);
+            gm &= gm - 1;
+            const int cbase =
+                32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw);
+            const float4 v = *reinterpret_cast<const float4*>(rowp + cbase);
+            const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t kx = key_of(xs[e]);
+              if (kx >= lb) insert8(T, pack(kx, cbase + e));
+            }
+          }
+        }
+      }
+
+      // ---- the tile is consumed: refill its slot with local tile k + kSlots ------------------
+      // (generic-proxy accesses to the slot are ordered before the bulk copy that overwrites it)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (t == 0 && ok && k + kSlots < nk) {
+        issue(k + kSlots);
+        __threadfence_block();
+        seq[slot] = k + kSlots;
+      }
+
+      // ======== phase 2: weights, fold and store from registers and the tables ===============
+      if (ok) {
+        int id[kK];
+        float val[kK];
+#pragma unroll
+        for (int s = 0; s < kK; ++s) {
+          id[s] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(T[s]));
+          val[s] = float_of_key(static_cast<uint32_t>(T[s] >> 32));
+        }
+        // fold targets: slot j >= P folds onto the first retained q of minimal loss; the scales
+        // of the targets are gathered from L2 while the weights are computed
+        float best[kK], scale[kK];
+        int fp[kK];
+        if (FOLD != kFoldNone) {
+#pragma unroll
+          for (int j = P; j < kK; ++j) {
+            const float* lrow = sm.loss + id[j] * kE;
+            float b = lrow[id[0]];
+            int pos = 0, tgt = id[0];
+#pragma unroll
+            for (int q = 1; q < P; ++q) {
+              const float lq = lrow[id[q]];
+              if (lq < b) {
+                b = lq;
+                pos = q;
+                tgt = id[q];
+              }
+            }
+            best[j] = b;
+            fp[j] = pos;
+            scale[j] = __ldg(coeff + id[j] * kE + tgt);
+          }
+        }
+
+        float w[kK];
+        {
+          float norm = 0.0f;
+#pragma unroll
+          for (int s = 0; s < kK; ++s) {
+            w[s] = exact_exp(__fsub_rn(val[s], val[0]));
+            norm = __fadd_rn(norm, w[s]);
+          }
+#pragma unroll
+          for (int s = 0; s < kK; ++s) {
+            float x = __fdiv_rn(w[s], norm);
+            if (p.scaling != 1.0f) x = __fmul_rn(x, p.scaling);
+            w[s] = x;
+          }
+        }
+
+        if (FOLD == kFoldNone) {
+          if (valid) {
+            float4* ow = reinterpret_cast<float4*>(p.out_w + row * kK);
+            int4* oi = reinterpret_cast<int4*>(p.out_ids + row * kK);
+            ow[0] = make_float4(w[0], w[1], w[2], w[3]);
+            ow[1] = make_float4(w[4], w[5], w[6], w[7]);
+            oi[0] = make_int4(id[0], id[1], id[2], id[3]);
+            oi[1] = make_int4(id[4], id[5], id[6], id[7]);
+          }
+        } else {
+          // ---- Qwen3 prefill fold: transfers added to their targets in slot order -------------
+          float ft[kK];
+#pragma unroll
+          for (int j = P; j < kK; ++j) ft[j] = __fmul_rn(w[j], best[j] < 1.0e30f ? scale[j] : 0.0f);
+          float acc[P];
+#pragma unroll
+          for (int q = 0; q < P; ++q) {
+            float a = w[q];
+#pragma unroll
+            for (int j = P; j < kK; ++j) a = __fadd_rn(a, q == fp[j] ? ft[j] : 0.0f);
+            acc[q] = a;
+          }
+          if (valid) {
+            if constexpr (P == 4) {
+              *reinterpret_cast<float4*>(p.out_w + row * P) =
+                  make_float4(acc[0], acc[1], acc[2], acc[3]);
+              *reinterpret_cast<int4*>(p.out_ids + row * P) =
+                  make_int4(id[0], id[1], id[2], id[3]);
+            } else {
+#pragma unroll
+              for (int q = 0; q < P; ++q) {
+                p.out_w[row * P + q] = acc[q];
+                p.out_ids[row * P + q] = id[q];
+              }
+            }
+          }
+        }
+      } else if (valid) {
+        // the tile never arrived: mark the routes invalid rather than leave stale values
+        const int width = FOLD == kFoldNone ? kK : P;
+        for (int q = 0; q < width; ++q) {
+          p.out_w[row * width + q] = 0.0f;
+          p.out_ids[row * width + q] = -1;
+        }
+      }
+    }
+    // this layer's table reads are ordered before the copy of the next layer's table
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    ks = ke;
+  }
+
+  // copies still in flight after a time-out land before the CTA's shared memory is released
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s)
+      if (sm.seq[s] > sm.done[s])
+        bar_wait(&sm.bar[s], static_cast<uint32_t>(sm.seq[s] / kSlots) & 1u);
+    if (table_pending >= 0) bar_wait(&sm.tbar, static_cast<uint32_t>(table_pending) & 1u);
+  }
+}
+
+template <int FOLD, int P>
+cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
+  auto kern = router_tpt_kernel<FOLD, P>;
+  static std::mutex mu;
+  static bool allowed[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!allowed[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kTptSmemBytes));
+      if (e != cudaSuccess) return e;
+      allowed[dev] = true;
+    }
+  }
+  int64_t blocks = (p.tokens + kRows - 1) / kRows * p.layers;
+  const int sms = sm_count();
+  if (sms > 0 && blocks > sms) blocks = sms;
+  if (blocks < 1) blocks = 1;
+  kern<<<static_cast<unsigned>(blocks), kWarps * 32, kTptSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+
+bool router_tpt_eligible(int experts, int scoring, int fold, const RouterParams& p) {
+  return experts == kE && scoring == EXF_SOFTMAX && fold != kFoldDsv4 && p.top_k == kK &&
+         p.renormalize && p.target_k >= 1 && p.target_k <= kK && aligned16(p.logits) &&
+         aligned16(p.out_w) && aligned16(p.out_ids) &&
+         (fold == kFoldNone || aligned16(p.sel_loss));
+}
+
+cudaError_t launch_router_tpt(int fold, const RouterParams& p, cudaStream_t stream) {
+  if (fold == kFoldNone) return launch_tpt<kFoldNone, kK>(p, stream);
+  switch (p.target_k) {
+    case 1: return launch_tpt<kFoldQwen3, 1>(p, stream);
+    case 2: return launch_tpt<kFoldQwen3, 2>(p, stream);
+    case 3: return launch_tpt<kFoldQwen3, 3>(p, stream);
+    case 4: return launch_tpt<kFoldQwen3, 4>(p, stream);
+    case 5: return launch_tpt<kFoldQwen3, 5>(p, stream);
+    case 6: return launch_tpt<kFoldQwen3, 6>(p, stream);
+    case 7: return launch_tpt<kFoldQwen3, 7>(p, stream);
+    default: return launch_tpt<kFoldQwen3, 8>(p, stream);
+  }
+}
+
+}  // namespace exf

@@ -83,6 +83,35 @@ def test_router_options(scoring):
         np.testing.assert_allclose(host(w), ew, rtol=1e-6, atol=0)
 
 
+@pytest.mark.parametrize("experts", [64, 128, 256, 512])
+def test_router_quantised_logits_tie_often(experts):
+    """Logits on coarse grids tie inside the top-k on many tokens (a candidate equal to another
+    candidate, to its own group maximum, or to the threshold); rows of mostly negative logits put
+    zeros of both signs among the candidates; half-precision rows tie now and then.  Ids and
+    weights stay bit-exact, also through the fused fold and over a ragged last tile."""
+    x = W.logits(77 + experts, 4099, experts)
+    x[1024:2048] = np.round(x[1024:2048] * 64) / 64       # ties within the top 8 on most rows
+    x[2048:3072] = np.round(x[2048:3072] * 8) / 8         # ties with the threshold
+    neg = -np.abs(x[3072:3584])
+    neg[:, ::5] = 0.0
+    neg[:, 1::7] = -0.0
+    x[3072:3584] = neg
+    x[3584:] = x[3584:].astype(np.float16).astype(np.float32)
+    lay = W.layer("qwen3_prefill")
+    coeff = np.resize(lay.coeff, (experts, experts)).astype(np.float32)
+    loss = np.resize(lay.loss, (experts, experts)).astype(np.float32)
+    for k in (8, 4):
+        w, ids = ops.router_topk(cuda(x), k, "softmax")
+        ew, ei = O.router_topk(x, k, "softmax")
+        np.testing.assert_array_equal(host(ids), ei)
+        np.testing.assert_array_equal(host(w), ew)
+        for keep in (k // 2, 3):
+            fw, fi = ops.router_fold_prefill(cuda(x), k, keep, cuda(coeff), cuda(loss))
+            efw, efi = O.router_fold(x, k, keep, coeff, loss)
+            np.testing.assert_array_equal(host(fi), efi)
+            np.testing.assert_array_equal(host(fw), efw)
+
+
 def test_router_ties_constant_rows_and_specials():
     """Exact ties take the lower expert id; constant rows, +-inf and NaN stay in range."""
     x = W.logits(5, 256, 128)
