@@ -12,12 +12,15 @@
 //   * Selection keys are IEEE totalOrder keys of the logits.  The 32 groups of 4 consecutive
 //     columns give 32 group maxima; their keys, with the low 5 bits replaced by the group's slot,
 //     go through a sorting network (4 x 19-comparator sorts, 3 merges) whose top 8 name the 8
-//     groups with the largest maxima.  Those groups are reloaded, their exact maxima sorted as
-//     (key desc, column asc), and every other element of those groups that reaches the 8th
-//     maximum is inserted.  When exactly 8 groups reach the 8th maximum and it is positive, this
-//     is the exact top 8 (every element that reaches it lies in those groups; no zeros, so -0 and
-//     +0 cannot tie).  Other tokens (ties of group maxima, zeros among the candidates) insert
-//     every element of every group that reaches the truncated bound instead: exact, slower.
+//     groups with the largest maxima.  Those groups are reloaded (their exact maxima are then
+//     in descending order unless two truncated keys tie; then they are sorted as (key desc,
+//     column asc)), and every other element of those groups that reaches the 8th maximum is
+//     inserted.  When the 9th largest maximum (the largest value the merges drop) is below the
+//     8th in its truncated key and the 8th maximum is positive, this is the exact top 8 (every
+//     element that reaches it lies in those groups; no zeros, so -0 and +0 cannot tie).  Other
+//     tokens (a group outside the 8 close to the 8th maximum, zeros among the candidates, NaN)
+//     insert every element of every group that reaches the truncated bound instead (every
+//     element, for a row with a NaN): exact, slower.
 //   * The fold's loss lookups (4 per omitted route) go to a shared-memory copy of the layer's
 //     128 x 128 loss table, loaded once per CTA and layer: scattered 4-byte reads from L1/L2 cost
 //     one pass per distinct line (32 per warp instruction), shared memory only its bank
@@ -37,8 +40,14 @@ namespace {
 
 constexpr int kE = 128;
 constexpr int kK = 8;
-constexpr int kWarps = 8;                // warps per CTA, each ranking one tile at a time
-constexpr int kSlots = 10;               // tile slots per CTA: a ring shared by its warps
+#ifndef EXF_TPT_WARPS
+#define EXF_TPT_WARPS 8
+#endif
+#ifndef EXF_TPT_SLOTS
+#define EXF_TPT_SLOTS 10
+#endif
+constexpr int kWarps = EXF_TPT_WARPS;    // warps per CTA, each ranking one tile at a time
+constexpr int kSlots = EXF_TPT_SLOTS;    // tile slots per CTA: a ring shared by its warps
 constexpr int kRows = 32;                // tokens per tile: one per lane
 constexpr int kTileFloats = kRows * kE;  // 16 KB
 constexpr uint32_t kSpinLimit = 1u << 20;
@@ -95,6 +104,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// max that returns NaN when either input is NaN
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 __device__ __forceinline__ void cx32(uint32_t& a, uint32_t& b) {
   const uint32_t hi = max(a, b), lo = min(a, b);
   a = hi;
@@ -116,10 +131,14 @@ __device__ __forceinline__ void sort8(T* v) {
   CX(v[1], v[4]); CX(v[3], v[6]);
   CX(v[1], v[2]); CX(v[3], v[4]); CX(v[5], v[6]);
 }
-// a, b sorted descending -> a = the 8 largest of both, sorted descending.
-__device__ __forceinline__ void merge8(uint32_t* a, const uint32_t* b) {
+// a, b sorted descending -> a = the 8 largest of both, sorted descending; dmax = the largest of
+// the values dropped so far (over a whole merge tree: the 9th largest input)
+__device__ __forceinline__ void merge8(uint32_t* a, const uint32_t* b, uint32_t& dmax) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = max(a[i], b[7 - i]);
+  for (int i = 0; i < 8; ++i) {
+    dmax = max(dmax, min(a[i], b[7 - i]));
+    a[i] = max(a[i], b[7 - i]);
+  }
   cx32(a[0], a[4]); cx32(a[1], a[5]); cx32(a[2], a[6]); cx32(a[3], a[7]);
   cx32(a[0], a[2]); cx32(a[1], a[3]); cx32(a[4], a[6]); cx32(a[5], a[7]);
   cx32(a[0], a[1]); cx32(a[2], a[3]); cx32(a[4], a[5]); cx32(a[6], a[7]);
@@ -239,25 +258,27 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
       // ======== phase 1: the selection, the only part that reads the tile =====================
       if (ok) {
         // ---- group maxima (slot u = 8 s + i holds columns 32 s + 4 (i ^ sw) .. + 3) ---------
-        uint32_t gmx[32];
+        // A float maximum keyed once equals the key maximum except that -0 may stand for +0
+        // (harmless: zeros never reach the fast path's theta, and the exact path merges them);
+        // a NaN makes the group's key all ones, which the exact path below takes over.  The key
+        // keeps its high 27 bits; the low 5 name the slot.
+        uint32_t pk[32];
 #pragma unroll
         for (int s = 0; s < 4; ++s)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 v = *reinterpret_cast<const float4*>(rowp + 32 * s + 4 * (i ^ sw));
-            gmx[8 * s + i] = max(max(order_key(v.x), order_key(v.y)),
-                                 max(order_key(v.z), order_key(v.w)));
+            const uint32_t g = order_key(fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
+            pk[8 * s + i] = (g & ~31u) | (31u - (8 * s + i));
           }
-        uint32_t pk[32];
-#pragma unroll
-        for (int u = 0; u < 32; ++u) pk[u] = (gmx[u] & ~31u) | (31u - u);
         sort8<uint32_t, cx32>(pk);
         sort8<uint32_t, cx32>(pk + 8);
         sort8<uint32_t, cx32>(pk + 16);
         sort8<uint32_t, cx32>(pk + 24);
-        merge8(pk, pk + 8);
-        merge8(pk + 16, pk + 24);
-        merge8(pk, pk + 16);
+        uint32_t p9 = 0;  // the 9th largest packed maximum
+        merge8(pk, pk + 8, p9);
+        merge8(pk + 16, pk + 24, p9);
+        merge8(pk, pk + 16, p9);
 
         // ---- the 8 named groups: exact maxima, sorted by (key desc, column asc) -------------
         uint32_t ek[kK][4];
@@ -275,12 +296,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
           emax[i] = ek[i][0] == m ? 0 : (ek[i][1] == m ? 1 : (ek[i][2] == m ? 2 : 3));
           T[i] = pack(m, cb[i] + emax[i]);
         }
-        sort8<uint64_t, cx64>(T);
-        const uint32_t theta = static_cast<uint32_t>(T[kK - 1] >> 32);
-        int reach = 0;
+        // distinct truncated keys: the exact maxima are already in descending order
+        bool distinct = true;
 #pragma unroll
-        for (int u = 0; u < 32; ++u) reach += gmx[u] >= theta ? 1 : 0;
-        const bool fast = reach == kK && theta > kKeyPosZero;
+        for (int i = 0; i + 1 < kK; ++i) distinct = distinct && (pk[i] >> 5) != (pk[i + 1] >> 5);
+        if (!distinct) sort8<uint64_t, cx64>(T);
+        const uint32_t theta = static_cast<uint32_t>(T[kK - 1] >> 32);
+        // every other group's truncated maximum below the 8th: each element that reaches theta
+        // lies in the 8 named groups
+        const bool apart = (p9 >> 5) < (pk[kK - 1] >> 5);
+        const bool nan_row = pk[0] >= 0xFFFFFFE0u;
+        const bool fast = apart && theta > kKeyPosZero && !nan_row;
 
         if (fast) {
           // other elements of the named groups that reach theta, listed in this lane's own row
@@ -298,12 +324,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
           for (int m = 0; m < nx; ++m) insert8(T, xl[(t + m) & 63]);
         } else if (valid) {
           // exact insertion over every element of every group whose maximum reaches the bound
-          // (pk[7] truncated is below the 8th largest key; -0 ranks equal to +0)
-          const uint32_t lb = pk[kK - 1] & ~31u;
+          // (pk[7] truncated is below the 8th largest key; -0 ranks equal to +0); a row with a
+          // NaN inserts every element
+          const uint32_t lb = nan_row ? 0u : pk[kK - 1] & ~31u;
           uint32_t gm = 0;
 #pragma unroll
           for (int u = 0; u < 32; ++u) {
-            const uint32_t gk = gmx[u] == kKeyNegZero ? kKeyPosZero : gmx[u];
+            const float4 v = *reinterpret_cast<const float4*>(
+                rowp + 32 * (u >> 3) + 4 * ((u & 7) ^ sw));
+            const uint32_t gk = max(max(key_of(v.x), key_of(v.y)), max(key_of(v.z), key_of(v.w)));
             gm |= (gk >= lb ? 1u : 0u) << u;
           }
 #pragma unroll
