@@ -152,6 +152,27 @@ __device__ __forceinline__ uint64_t pack(uint32_t key, int col) {
   return (static_cast<uint64_t>(key) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(col));
 }
 
+// Exact top 8 of one row by insertion of every element (key at least lb) of every group whose
+// maximum reaches lb; -0 ranks equal to +0.  Out of line: rarely taken, and kept out of the
+// instruction cache of the hot loop.
+__device__ __noinline__ void exact_top8(const float* rowp, int sw, uint32_t lb, uint64_t* out) {
+  uint64_t T[kK];
+#pragma unroll
+  for (int q = 0; q < kK; ++q) T[q] = 0;
+#pragma unroll 1
+  for (int u = 0; u < 32; ++u) {
+    const int cbase = 32 * (u >> 3) + 4 * ((u & 7) ^ sw);
+    const float4 v = *reinterpret_cast<const float4*>(rowp + cbase);
+    const uint32_t k[4] = {key_of(v.x), key_of(v.y), key_of(v.z), key_of(v.w)};
+    if (max(max(k[0], k[1]), max(k[2], k[3])) < lb) continue;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (k[e] >= lb) insert8(T, pack(k[e], cbase + e));
+  }
+#pragma unroll
+  for (int q = 0; q < kK; ++q) out[q] = T[q];
+}
+
 template <int FOLD, int P>
 __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const RouterParams p) {
   extern __shared__ uint8_t tpt_raw[];
@@ -309,47 +330,36 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
         const bool fast = apart && theta > kKeyPosZero && !nan_row;
 
         if (fast) {
-          // other elements of the named groups that reach theta, listed in this lane's own row
-          // (its logits are no longer needed); the entry offset by lane keeps bank pairs apart
-          uint64_t* xl = reinterpret_cast<uint64_t*>(rowp);
-          int nx = 0;
+          // other elements of the named groups that reach theta: a mask over the 32 (group,
+          // element) sites, each inserted after a reload from the tile (typically 0-2 of them)
+          uint32_t xm = 0, slo = 0, shi = 0;
 #pragma unroll
-          for (int i = 0; i < kK; ++i)
+          for (int i = 0; i < kK; ++i) {
+            const uint32_t u = 31u - (pk[i] & 31u);
+            if (i < 6)
+              slo |= u << (5 * i);
+            else
+              shi |= u << (5 * (i - 6));
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              if (e != emax[i] && ek[i][e] >= theta) {
-                xl[(t + nx) & 63] = pack(ek[i][e], cb[i] + e);
-                ++nx;
-              }
-          for (int m = 0; m < nx; ++m) insert8(T, xl[(t + m) & 63]);
+              xm |= (e != emax[i] && ek[i][e] >= theta ? 1u : 0u) << (4 * i + e);
+          }
+          while (xm) {
+            const int site = __ffs(xm) - 1;
+            xm &= xm - 1;
+            const int i = site >> 2;
+            const uint32_t u = (i < 6 ? slo >> (5 * i) : shi >> (5 * (i - 6))) & 31u;
+            const int col =
+                32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw) + (site & 3);
+            insert8(T, pack(order_key(rowp[col]), col));
+          }
         } else if (valid) {
           // exact insertion over every element of every group whose maximum reaches the bound
-          // (pk[7] truncated is below the 8th largest key; -0 ranks equal to +0); a row with a
-          // NaN inserts every element
-          const uint32_t lb = nan_row ? 0u : pk[kK - 1] & ~31u;
-          uint32_t gm = 0;
+          // (pk[7] truncated is below the 8th largest key); a row with a NaN inserts every element
+          uint64_t Te[kK];
+          exact_top8(rowp, sw, nan_row ? 0u : pk[kK - 1] & ~31u, Te);
 #pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            const float4 v = *reinterpret_cast<const float4*>(
-                rowp + 32 * (u >> 3) + 4 * ((u & 7) ^ sw));
-            const uint32_t gk = max(max(key_of(v.x), key_of(v.y)), max(key_of(v.z), key_of(v.w)));
-            gm |= (gk >= lb ? 1u : 0u) << u;
-          }
-#pragma unroll
-          for (int q = 0; q < kK; ++q) T[q] = 0;
-          while (gm) {
-            const uint32_t u = static_cast<uint32_t>(__ffs(gm) - 1);
-            gm &= gm - 1;
-            const int cbase =
-                32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw);
-            const float4 v = *reinterpret_cast<const float4*>(rowp + cbase);
-            const float xs[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t kx = key_of(xs[e]);
-              if (kx >= lb) insert8(T, pack(kx, cbase + e));
-            }
-          }
+          for (int q = 0; q < kK; ++q) T[q] = Te[q];
         }
       }
 
