@@ -200,6 +200,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
     bar_expect(&sm.bar[slot], bytes);
     bulk_load(sm.tile[slot], p.logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
   };
+  // Launched as a programmatic dependent of the previous kernel in the stream: let the next
+  // launch's CTAs take SMs as this grid's CTAs exit, and wait here until the previous grid has
+  // completed and its writes are visible (a no-op for an ordinary launch).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
       bar_init(&sm.bar[s]);
@@ -507,8 +512,18 @@ cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
   const int sms = sm_count();
   if (sms > 0 && blocks > sms) blocks = sms;
   if (blocks < 1) blocks = 1;
-  kern<<<static_cast<unsigned>(blocks), kWarps * 32, kTptSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = kTptSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
