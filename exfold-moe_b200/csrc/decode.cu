@@ -2,7 +2,8 @@
 //
 // decode_kernel is one CTA of 1024 threads doing the whole transform for a decode batch:
 //   1. importance[e] = sum over routes of w * norm[e] as 2^-32 fixed point in int64 (shared-
-//      memory 64-bit atomics: exact, so independent of the order the atomics land in), or
+//      memory 64-bit atomics into per-warp-group copies, then summed: exact, so independent of
+//      the order the atomics land in), or
 //      read from a caller-reduced vector (batch sharded over GPUs), or skipped when the caller
 //      gives the subset explicitly;
 //   2. order = experts by (importance desc, expert asc), E/ (1024/E) comparisons per thread;
@@ -26,14 +27,29 @@ constexpr int kMaxExperts = 1024;
 
 
 
+constexpr int kRouteUnroll = 8;   // routes per thread with their loads in flight together
+constexpr int kTableBatch = 4;    // source experts per warp with their loss reads in flight together
+
+// Private importance histograms during phase 1: kHistInts 64-bit counters shared out as
+// 2048 / E copies, one per group of warps, so that the (compare-and-swap) 64-bit shared atomics
+// only collide within a warp; they alias the arrays that phase 1 does not use.
+constexpr int kHistLongs = 2048;
+
 struct DecodeSmem {
   long long imp[kMaxExperts];
-  int order[kMaxExperts];
-  int rank[kMaxExperts];
-  int tgt[kMaxExperts];
-  float scale[kMaxExperts];
+  float norm[kMaxExperts];
+  union {
+    long long hist[kHistLongs];
+    struct {
+      int order[kMaxExperts];
+      int rank[kMaxExperts];
+      int tgt[kMaxExperts];
+      float scale[kMaxExperts];
+    };
+  };
   unsigned char keep[kMaxExperts];
 };
+static_assert(sizeof(long long) * kHistLongs <= 4 * 4 * kMaxExperts, "hist alias");
 
 // Sequential strict-< argmin semantics as a (value, position) reduction.
 //   Qwen3 (exfold/qwen3/kernels.py:186-212): start from position 0; later NaNs never win, so
@@ -57,17 +73,39 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   const IT* ids = static_cast<const IT*>(p.ids);
 
   // ---- 1. importance ------------------------------------------------------------------------
+  const int copies = kHistLongs / E < 32 ? kHistLongs / E : 32;  // >= 2 for E <= 1024
+  long long* hist = sm.hist + ((tid >> 5) % copies) * E;
   for (int e = tid; e < E; e += kDecodeThreads) {
     sm.imp[e] = (p.source == kImportanceGiven) ? p.importance[e] : 0;
+    if (p.source == kImportanceFromRoutes) sm.norm[e] = __ldg(p.norms + e);
     sm.keep[e] = 0;
   }
+  if (p.source == kImportanceFromRoutes)
+    for (int i = tid; i < copies * E; i += kDecodeThreads) sm.hist[i] = 0;
   __syncthreads();
   if (p.source == kImportanceFromRoutes) {
-    for (int64_t r = tid; r < p.routes; r += kDecodeThreads) {
-      const int e = (int)ids[r];
-      if (e < 0 || e >= E) continue;
-      const long long q = fixed_point(__fmul_rn(to_f32(w[r]), __ldg(p.norms + e)));
-      atomicAdd(reinterpret_cast<unsigned long long*>(&sm.imp[e]), (unsigned long long)q);
+    for (int64_t base = 0; base < p.routes; base += kRouteUnroll * kDecodeThreads) {
+      WT wr[kRouteUnroll];
+      int er[kRouteUnroll];
+#pragma unroll
+      for (int j = 0; j < kRouteUnroll; ++j) {
+        const int64_t r = base + j * kDecodeThreads + tid;
+        er[j] = r < p.routes ? (int)ids[r] : -1;
+        wr[j] = r < p.routes ? w[r] : from_f32<WT>(0.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < kRouteUnroll; ++j) {
+        const int e = er[j];
+        if (e < 0 || e >= E) continue;
+        const long long q = fixed_point(__fmul_rn(to_f32(wr[j]), sm.norm[e]));
+        atomicAdd(reinterpret_cast<unsigned long long*>(&hist[e]), (unsigned long long)q);
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kDecodeThreads) {
+      long long acc = 0;
+      for (int c = 0; c < copies; ++c) acc += sm.hist[c * E + e];
+      sm.imp[e] = acc;
     }
     __syncthreads();
   }
@@ -113,58 +151,86 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   }
 
   // ---- 3. target table ----------------------------------------------------------------------
+  // A warp builds the rows of kTableBatch source experts at once: their loss reads are issued
+  // together, the first and the chosen loss come out of the reduction, and only the scale of
+  // each chosen target is a second round trip.
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  for (int e = warp; e < E; e += kDecodeThreads / 32) {
-    const float* lrow = p.loss + (int64_t)e * E;
-    int tgt = e;
-    float scale = 1.0f;
-    if (p.variant == EXF_QWEN3) {
-      float v = INFINITY;
-      int pos = 0x7fffffff;
-      for (int q = lane; q < D; q += 32) {
-        const float c = __ldg(lrow + sm.order[q]);
-        const float cv = (c != c) ? INFINITY : c;
-        if (cv < v) {
-          v = cv;
-          pos = q;
+  constexpr int kWarps = kDecodeThreads / 32;
+  const bool qwen3 = p.variant == EXF_QWEN3;
+  for (int e0 = warp; e0 < E; e0 += kTableBatch * kWarps) {
+    int ex[kTableBatch];
+    bool act[kTableBatch];
+    float v[kTableBatch], first[kTableBatch];
+    int pos[kTableBatch];
+#pragma unroll
+    for (int i = 0; i < kTableBatch; ++i) {
+      ex[i] = e0 + i * kWarps;
+      act[i] = ex[i] < E && (qwen3 || (!sm.keep[ex[i]] && sm.imp[ex[i]] > 0));
+      v[i] = INFINITY;
+      pos[i] = 0x7fffffff;
+      first[i] = 0.0f;
+    }
+    for (int q = lane; q < D; q += 32) {
+      const int o = sm.order[q];
+      const bool use = qwen3 || sm.imp[o] > 0;
+      float c[kTableBatch];
+#pragma unroll
+      for (int i = 0; i < kTableBatch; ++i)
+        c[i] = (act[i] && use) ? __ldg(p.loss + (int64_t)ex[i] * E + o) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < kTableBatch; ++i) {
+        if (!act[i] || !use) continue;
+        if (qwen3) {
+          // exfold/qwen3/kernels.py:186-212: NaN never wins after position 0
+          if (q == 0) first[i] = c[i];
+          const float cv = (c[i] != c[i]) ? INFINITY : c[i];
+          if (cv < v[i]) {
+            v[i] = cv;
+            pos[i] = q;
+          }
+        } else if (c[i] < FLT_MAX && c[i] < v[i]) {  // exfold_kernels.cu:175-187
+          v[i] = c[i];
+          pos[i] = q;
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < kTableBatch; ++i) {
       for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-        const int op = __shfl_xor_sync(0xffffffffu, pos, off);
-        argmin_merge(v, pos, ov, op);
+        const float ov = __shfl_xor_sync(0xffffffffu, v[i], off);
+        const int op = __shfl_xor_sync(0xffffffffu, pos[i], off);
+        argmin_merge(v[i], pos[i], ov, op);
       }
-      const float first = __ldg(lrow + sm.order[0]);
-      if (first != first || pos == 0x7fffffff) pos = 0;
-      tgt = sm.order[pos];
-      const float best = __ldg(lrow + tgt);
-      scale = (best < 1.0e30f) ? __ldg(p.coeff + (int64_t)e * E + tgt) : 0.0f;
-    } else if (!sm.keep[e] && sm.imp[e] > 0) {
-      float v = INFINITY;
-      int pos = 0x7fffffff;
-      for (int q = lane; q < D; q += 32) {
-        const int o = sm.order[q];
-        if (sm.imp[o] <= 0) continue;
-        const float c = __ldg(lrow + o);
-        if (c < FLT_MAX && c < v) {
-          v = c;
-          pos = q;
+      first[i] = __shfl_sync(0xffffffffu, first[i], 0);  // position 0 is lane 0's
+    }
+    float sc[kTableBatch];
+    int tg[kTableBatch];
+#pragma unroll
+    for (int i = 0; i < kTableBatch; ++i) {
+      tg[i] = ex[i];
+      sc[i] = 1.0f;
+      if (!act[i]) continue;
+      if (qwen3) {
+        float best = v[i];  // finite whenever a position won on its own
+        if (first[i] != first[i] || pos[i] == 0x7fffffff) {
+          pos[i] = 0;
+          best = first[i];
         }
-      }
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-        const int op = __shfl_xor_sync(0xffffffffu, pos, off);
-        argmin_merge(v, pos, ov, op);
-      }
-      if (pos != 0x7fffffff) {
-        tgt = sm.order[pos];
-        scale = (tgt == e) ? 1.0f : __ldg(p.coeff + (int64_t)e * E + tgt);
+        tg[i] = sm.order[pos[i]];
+        sc[i] = (best < 1.0e30f) ? __ldg(p.coeff + (int64_t)ex[i] * E + tg[i]) : 0.0f;
+      } else if (pos[i] != 0x7fffffff) {
+        tg[i] = sm.order[pos[i]];
+        sc[i] = (tg[i] == ex[i]) ? 1.0f : __ldg(p.coeff + (int64_t)ex[i] * E + tg[i]);
       }
     }
     if (lane == 0) {
-      sm.tgt[e] = tgt;
-      sm.scale[e] = scale;
+#pragma unroll
+      for (int i = 0; i < kTableBatch; ++i)
+        if (ex[i] < E) {
+          sm.tgt[ex[i]] = tg[i];
+          sm.scale[ex[i]] = sc[i];
+        }
     }
   }
   __syncthreads();
@@ -172,26 +238,37 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   // ---- 4. apply -----------------------------------------------------------------------------
   WT* ow = static_cast<WT*>(p.out_w);
   IT* oi = static_cast<IT*>(p.out_ids);
-  for (int64_t r = tid; r < p.routes; r += kDecodeThreads) {
-    const IT raw = ids[r];
-    const int e = (int)raw;
-    const WT wr = w[r];
-    if (e < 0 || e >= E) {
-      ow[r] = wr;
-      oi[r] = raw;
-    } else if (p.variant == EXF_QWEN3) {
-      if (sm.keep[e]) {
-        ow[r] = wr;
-        oi[r] = raw;
+  for (int64_t base = 0; base < p.routes; base += kRouteUnroll * kDecodeThreads) {
+    IT raw[kRouteUnroll];
+    WT wr[kRouteUnroll];
+#pragma unroll
+    for (int j = 0; j < kRouteUnroll; ++j) {
+      const int64_t r = base + j * kDecodeThreads + tid;
+      raw[j] = r < p.routes ? ids[r] : (IT)-1;
+      wr[j] = r < p.routes ? w[r] : from_f32<WT>(0.0f);
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteUnroll; ++j) {
+      const int64_t r = base + j * kDecodeThreads + tid;
+      if (r >= p.routes) continue;
+      const int e = (int)raw[j];
+      if (e < 0 || e >= E) {
+        ow[r] = wr[j];
+        oi[r] = raw[j];
+      } else if (qwen3) {
+        if (sm.keep[e]) {
+          ow[r] = wr[j];
+          oi[r] = raw[j];
+        } else {
+          // exfold/qwen3/kernels.py:214-225: the scale is cast to the weight dtype first
+          const float s = to_f32(from_f32<WT>(sm.scale[e]));
+          ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr[j]), s));
+          oi[r] = (IT)sm.tgt[e];
+        }
       } else {
-        // exfold/qwen3/kernels.py:214-225: the scale is cast to the weight dtype first
-        const float s = to_f32(from_f32<WT>(sm.scale[e]));
-        ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr), s));
+        ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr[j]), sm.scale[e]));
         oi[r] = (IT)sm.tgt[e];
       }
-    } else {
-      ow[r] = from_f32<WT>(__fmul_rn(to_f32(wr), sm.scale[e]));
-      oi[r] = (IT)sm.tgt[e];
     }
   }
 }
