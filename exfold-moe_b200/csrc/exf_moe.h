@@ -18,6 +18,9 @@ struct ExpertGemmParams {
   int hidden;
   int k;                       // reduction length of this GEMM
   int n_total;                 // GEMM-1: intermediate size; GEMM-2: hidden size
+  int n_tiles;                 // output tiles per 128-row block
+  int m_blocks;                // 128-row blocks of the capacity (those past the padded count
+                               // are skipped on the device)
   int* status;                 // set to 1 if a pipeline wait timed out (may be null)
   __nv_bfloat16* act;          // GEMM-1 output [capacity][intermediate]
   const float* route_w;        // GEMM-2: [numel] routing weights

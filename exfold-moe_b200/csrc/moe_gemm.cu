@@ -8,12 +8,14 @@
 //   GEMM-2 : out[route, h] = w_route * (act[m] . W2[e, h])         (N = 256 tile of H)
 //   combine: y[t, h] = sum over the token's routes of out[route, h] (fixed order: deterministic)
 //
-// Both GEMMs share one mainloop: a CTA owns one 128 x 256 output tile of one expert; warp 0
-// streams 128 x 64 A and 256 x 64 B bf16 tiles with TMA (128-byte swizzle) through a 4-stage
-// mbarrier pipeline; one elected thread of warp 1 issues tcgen05.mma (M = 128, N = 256, K = 16,
-// fp32 accumulation in TMEM) and releases each stage with tcgen05.commit; warps 2-5 read the
-// accumulator with tcgen05.ld and run the epilogue.  The grid runs the N tiles of one M block
-// next to each other, so A tiles and the expert's weight tiles are reused from L2.
+// Both GEMMs share one mainloop in a persistent kernel: one CTA per SM walks 128 x 256 output
+// tiles (one expert each); warp 0 streams 128 x 64 A and 256 x 64 B bf16 tiles with TMA
+// (128-byte swizzle) through a 4-stage mbarrier ring that runs on across tiles; one elected
+// thread of warp 1 issues tcgen05.mma (M = 128, N = 256, K = 16, fp32 accumulation in TMEM) and
+// releases each stage with tcgen05.commit; warps 2-5 read the accumulator with tcgen05.ld and run
+// the epilogue.  Two TMEM accumulators (all 512 columns) let the epilogue of one tile overlap
+// the mainloop of the next.  The N tiles of one M block run side by side on neighbouring CTAs,
+// so A tiles and the expert's weight tiles are reused from L2.
 // Every mbarrier wait is bounded: on time-out the CTA records an error in *status, skips the
 // rest of its work, still frees its TMEM and returns.
 #include <cuda.h>
@@ -35,14 +37,16 @@ constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kGemmThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 512;       // two 256-column fp32 accumulators
 constexpr uint32_t kWaitLimit = 1u << 20;
 
 struct GemmSmem {
   alignas(1024) uint8_t tiles[kStages][kStageBytes];
   alignas(8) uint64_t full[kStages];
   alignas(8) uint64_t empty[kStages];
-  alignas(8) uint64_t acc_full;
+  alignas(8) uint64_t acc_full[2];   // accumulator b holds a finished tile
+  alignas(8) uint64_t acc_empty[2];  // the epilogue has read accumulator b
+  alignas(8) uint64_t drain;         // every MMA issued by the CTA has completed
   uint32_t tmem_base;
   int failed;
 };
@@ -59,6 +63,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                "r"(bytes)
                : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -169,21 +176,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x;
-  const int m_block = blockIdx.y;
 
-  // blocks past the padded route count, or of no expert, have nothing to do
+  // Tiles t = m_block * n_tiles + n_tile, strided over the persistent CTAs: the N tiles of one
+  // block run side by side (A and the expert's weights are reused from L2).  Blocks past the
+  // padded route count, or of no expert, are skipped by every role alike.
   const int post = *p.num_post_pad;
-  if (m_block * kBM >= post) return;
-  const int expert = p.expert_ids[m_block];
-  if (expert < 0 || expert >= p.experts) return;
+  const int m_used = (post + kBM - 1) / kBM < p.m_blocks ? (post + kBM - 1) / kBM : p.m_blocks;
+  const int ntiles = m_used * p.n_tiles;
+  auto tile_expert = [&](int t, int& m_block, int& n_tile) {
+    m_block = t / p.n_tiles;
+    n_tile = t - m_block * p.n_tiles;
+    const int e = p.expert_ids[m_block];
+    return (e >= 0 && e < p.experts) ? e : -1;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&sm.drain, 1);
     sm.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -196,78 +212,104 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kblocks = p.k / kBK;
 
   if (warp == 0) {
-    // ---- TMA producer
+    // ---- TMA producer: one stage ring across all of this CTA's tiles
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        if (!mbar_wait(&sm.empty[s], ((kb / kStages) & 1) ^ 1, failed)) break;
-        ++issued;
-        uint8_t* a_dst = sm.tiles[s];
-        uint8_t* b_dst = sm.tiles[s] + kATileBytes;
-        mbar_expect_tx(&sm.full[s], kStageBytes);
-        tma_load_2d(a_dst, &map_a, &sm.full[s], kb * kBK, m_block * kBM);
-        if (KIND == kGemmSwiGLU) {
-          // gate rows [n0, n0+128) and up rows [I + n0, I + n0 + 128) of W13[expert]
-          const int row0 = expert * 2 * p.n_total + n_tile * (kBN / 2);
-          tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, row0);
-          tma_load_2d(b_dst + kBTileBytes / 2, &map_b, &sm.full[s], kb * kBK, row0 + p.n_total);
-        } else {
-          tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, expert * p.n_total + n_tile * kBN);
+      uint32_t g = 0;  // k-blocks issued
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int m_block, n_tile;
+        const int expert = tile_expert(t, m_block, n_tile);
+        if (expert < 0) continue;
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kStages;
+          ok = mbar_wait(&sm.empty[s], ((g / kStages) & 1) ^ 1, failed);
+          if (!ok) break;
+          uint8_t* a_dst = sm.tiles[s];
+          uint8_t* b_dst = sm.tiles[s] + kATileBytes;
+          mbar_expect_tx(&sm.full[s], kStageBytes);
+          tma_load_2d(a_dst, &map_a, &sm.full[s], kb * kBK, m_block * kBM);
+          if (KIND == kGemmSwiGLU) {
+            // gate rows [n0, n0+128) and up rows [I + n0, I + n0 + 128) of W13[expert]
+            const int row0 = expert * 2 * p.n_total + n_tile * (kBN / 2);
+            tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, row0);
+            tma_load_2d(b_dst + kBTileBytes / 2, &map_b, &sm.full[s], kb * kBK,
+                        row0 + p.n_total);
+          } else {
+            tma_load_2d(b_dst, &map_b, &sm.full[s], kb * kBK, expert * p.n_total + n_tile * kBN);
+          }
         }
       }
-      if (*failed) {
-        // let this CTA's copies still in flight land before its shared memory is released
-        for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
-          mbar_wait_drain(&sm.full[kb % kStages], (kb / kStages) & 1);
-      }
+      // copies still in flight (only after a time-out) land before shared memory is released
+      for (uint32_t j = g > kStages ? g - kStages : 0; j < g; ++j)
+        mbar_wait_drain(&sm.full[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer (one thread)
+    // ---- MMA issuer (one thread): tile i accumulates into TMEM columns [256 (i & 1), +256)
     if (lane == 0) {
+      uint32_t g = 0;  // k-blocks consumed
+      int i = 0;       // tiles accumulated
       bool ok = true;
-      for (int kb = 0; kb < kblocks && ok; ++kb) {
-        const int s = kb % kStages;
-        ok = mbar_wait(&sm.full[s], (kb / kStages) & 1, failed);
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int m_block, n_tile;
+        if (tile_expert(t, m_block, n_tile) < 0) continue;
+        const int b = i & 1;
+        ok = mbar_wait(&sm.acc_empty[b], ((i >> 1) & 1) ^ 1, failed);
         if (!ok) break;
         fence_after_sync();
-        const uint32_t a_base = smem_addr(sm.tiles[s]);
-        const uint32_t b_base = a_base + kATileBytes;
+        const uint32_t acc = tmem + static_cast<uint32_t>(b * kBN);
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kStages;
+          ok = mbar_wait(&sm.full[s], (g / kStages) & 1, failed);
+          if (!ok) break;
+          fence_after_sync();
+          const uint32_t a_base = smem_addr(sm.tiles[s]);
+          const uint32_t b_base = a_base + kATileBytes;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)
-          mma_bf16(tmem, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
-                   (kb > 0 || k > 0) ? 1u : 0u);
-        mma_commit(&sm.empty[s]);
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_bf16(acc, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
+                     (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&sm.empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&sm.acc_full[b]);
+        ++i;
       }
-      mma_commit(&sm.acc_full);
+      // every MMA this thread issued has completed before TMEM is released
+      mma_commit(&sm.drain);
+      mbar_wait_drain(&sm.drain, 0);
     }
   } else {
     // ---- epilogue: warps 2-5 own TMEM lanes 32*(warp%4) .. +31, one output row per thread
     const int q = warp & 3;
-    const int row = m_block * kBM + q * 32 + lane;
-    const bool ok = mbar_wait(&sm.acc_full, 0, failed);
-    fence_after_sync();
-    if (ok && !*failed) {
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      int m_block, n_tile;
+      if (tile_expert(t, m_block, n_tile) < 0) continue;
+      const int b = i & 1;
+      const bool ok = mbar_wait(&sm.acc_full[b], (i >> 1) & 1, failed);
+      fence_after_sync();
+      if (!ok || *failed) break;
+      const int row = m_block * kBM + q * 32 + lane;
+      const uint32_t taddr = tmem + static_cast<uint32_t>(b * kBN) + ((uint32_t)(q * 32) << 16);
       if (KIND == kGemmSwiGLU) {
         // act[row, n0 + c] = silu(gate) * up; gate in columns [0,128), up in [128,256)
         __nv_bfloat16* dst = p.act + (int64_t)row * p.n_total + n_tile * (kBN / 2);
 #pragma unroll 1
         for (int c = 0; c < kBN / 2; c += 32) {
-          float g[32], u[32];
-          tmem_load32(taddr + c, g);
-          tmem_load32(taddr + kBN / 2 + c, u);
+          float gt[32], up[32];
+          tmem_load32(taddr + c, gt);
+          tmem_load32(taddr + kBN / 2 + c, up);
           uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = g[2 * i] / (1.0f + __expf(-g[2 * i])) * u[2 * i];
-            const float a1 = g[2 * i + 1] / (1.0f + __expf(-g[2 * i + 1])) * u[2 * i + 1];
-            packed[i] = pack_bf16(a0, a1);
+          for (int j = 0; j < 16; ++j) {
+            const float a0 = gt[2 * j] / (1.0f + __expf(-gt[2 * j])) * up[2 * j];
+            const float a1 = gt[2 * j + 1] / (1.0f + __expf(-gt[2 * j + 1])) * up[2 * j + 1];
+            packed[j] = pack_bf16(a0, a1);
           }
           uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          for (int j = 0; j < 4; ++j)
+            d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
         }
       } else {
         // out[route, n0 + c] = w_route * acc for real routes; padding rows are dropped.  The
@@ -284,22 +326,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (real) {
             uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(pack_bf16(v[8 * i] * wr, v[8 * i + 1] * wr),
-                                 pack_bf16(v[8 * i + 2] * wr, v[8 * i + 3] * wr),
-                                 pack_bf16(v[8 * i + 4] * wr, v[8 * i + 5] * wr),
-                                 pack_bf16(v[8 * i + 6] * wr, v[8 * i + 7] * wr));
+            for (int j = 0; j < 4; ++j)
+              d4[j] = make_uint4(pack_bf16(v[8 * j] * wr, v[8 * j + 1] * wr),
+                                 pack_bf16(v[8 * j + 2] * wr, v[8 * j + 3] * wr),
+                                 pack_bf16(v[8 * j + 4] * wr, v[8 * j + 5] * wr),
+                                 pack_bf16(v[8 * j + 6] * wr, v[8 * j + 7] * wr));
           }
         }
       }
+      // the accumulator has been read: the MMA thread may start the tile after next in it
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      ++i;
     }
   }
   fence_before_sync();
   __syncthreads();
   if (warp == 1) {
-    // the accumulator barrier completes once every issued MMA has finished (immediately on the
-    // normal path, where the epilogue already waited for it)
-    if (lane == 0) mbar_wait_drain(&sm.acc_full, 0);
     __syncwarp();
     fence_after_sync();
     tmem_free(tmem, kTmemCols);
@@ -416,6 +460,14 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// One CTA per SM (192 KB of pipeline stages and all 512 TMEM columns), never more than tiles.
+static unsigned persistent_tiles(const ExpertGemmParams& p) {
+  const int64_t tiles = (int64_t)p.m_blocks * p.n_tiles;
+  const int sms = sm_count();
+  int64_t g = sms > 0 && tiles > sms ? sms : tiles;
+  return (unsigned)(g > 0 ? g : 1);
+}
+
 int64_t moe_capacity(int64_t numel, int experts) {
   int64_t cap = numel + (int64_t)experts * (kBM - 1);
   cap = (cap + kBM - 1) / kBM * kBM;
@@ -487,8 +539,9 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
   p.k = a.hidden;
   p.n_total = a.inter;
   p.act = w.act;
-  dim3 g1((unsigned)(a.inter / (kBN / 2)), (unsigned)(cap / kBM));
-  expert_gemm_kernel<kGemmSwiGLU><<<g1, kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
+  p.m_blocks = (int)(cap / kBM);
+  p.n_tiles = a.inter / (kBN / 2);
+  expert_gemm_kernel<kGemmSwiGLU><<<persistent_tiles(p), kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // 4. GEMM-2, weighted per-route rows
@@ -499,8 +552,8 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
   p.n_total = a.hidden;
   p.route_w = a.topk_w;
   p.out = w.out;
-  dim3 g2((unsigned)(a.hidden / kBN), (unsigned)(cap / kBM));
-  expert_gemm_kernel<kGemmDown><<<g2, kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
+  p.n_tiles = a.hidden / kBN;
+  expert_gemm_kernel<kGemmDown><<<persistent_tiles(p), kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // 5. combine the routes of each token
