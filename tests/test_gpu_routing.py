@@ -112,6 +112,37 @@ def test_router_quantised_logits_tie_often(experts):
             np.testing.assert_array_equal(host(fw), efw)
 
 
+def test_router_sigmoid_e256_ties_and_options():
+    """Biased-sigmoid router at 256 experts on quantised logits and biases (exact key ties,
+    candidates within the approximate keys' margin of the threshold), without a bias, without
+    renormalisation and with scaling; and the fused DeepSeek fold in every renorm mode on the same
+    rows.  Ids and weights bit-exact."""
+    E = 256
+    x = W.logits(91, 4133, E)
+    x[1000:2000] = np.round(x[1000:2000] * 16) / 16
+    x[2000:3000] = np.round(x[2000:3000] * 2) / 2
+    bias = W.router_bias(91, E)
+    qbias = (np.round(bias * 8) / 8).astype(np.float32)
+    lay = W.layer("dsv4_prefill", tokens=64)
+    coeff, loss, conf = dsv4_tables(lay)
+    for b in (bias, qbias, None):
+        for renorm, scaling in ((True, 1.0), (False, 2.5)):
+            w, ids = ops.router_topk(cuda(x), 8, "sigmoid", None if b is None else cuda(b),
+                                     renormalize=renorm, scaling=scaling)
+            ew, ei = O.router_topk(x, 8, "sigmoid", b, renorm, scaling)
+            np.testing.assert_array_equal(host(ids), ei)
+            np.testing.assert_array_equal(host(w), ew)
+    for mode in (0, 1, 2):
+        for keep in (3, 5):
+            w, ids = ops.router_fold_prefill(cuda(x), 8, keep, cuda(coeff), cuda(loss),
+                                             scoring="sigmoid", bias=cuda(qbias), variant="dsv4",
+                                             renorm_mode=mode, conf_loss=cuda(conf))
+            ew, ei = O.router_fold(x, 8, keep, coeff, loss, scoring="sigmoid", bias=qbias,
+                                   variant="dsv4", conf_loss=conf, renorm_mode=mode)
+            np.testing.assert_array_equal(host(ids), ei)
+            np.testing.assert_array_equal(host(w), ew)
+
+
 def test_router_ties_constant_rows_and_specials():
     """Exact ties take the lower expert id; constant rows, +-inf and NaN stay in range."""
     x = W.logits(5, 256, 128)
