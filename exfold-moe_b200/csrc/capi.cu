@@ -91,8 +91,8 @@ static int router_common(const char* name, const float* logits, int64_t tokens, 
   EXF_REQUIRE(tokens >= 0 && layers >= 1, "%s: tokens must be >= 0 and layers >= 1", name);
   EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
   EXF_REQUIRE(experts >= top_k, "%s: experts (%d) < top_k (%d)", name, experts, top_k);
-  EXF_REQUIRE(scoring == EXF_SOFTMAX || scoring == EXF_SIGMOID, "%s: unknown scoring %d", name,
-              scoring);
+  EXF_REQUIRE(scoring == EXF_SOFTMAX || scoring == EXF_SIGMOID || scoring == EXF_SQRTSOFTPLUS,
+              "%s: unknown scoring %d", name, scoring);
   if (experts != 64 && experts != 128 && experts != 256 && experts != 512)
     return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be one of 64, 128, 256, 512 (got %d)", name,
                 experts);
@@ -114,6 +114,28 @@ EXF_API int exf_router_topk(const float* logits, int64_t tokens, int experts, in
   RouterParams p{logits, tokens, 1, top_k, bias, renormalize, scaling, top_k, 0,
                  nullptr, nullptr, nullptr, out_w, out_ids};
   return cuda_status(launch_router(experts, scoring, 0, p, (cudaStream_t)stream), "exf_router_topk");
+}
+
+EXF_API int exf_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
+                            int scoring, const void* token_ids, int id_dtype,
+                            const int32_t* table, int64_t table_rows, int renormalize,
+                            float scaling, float* out_w, int32_t* out_ids, exf_stream_t stream) {
+  const char* name = "exf_router_hash";
+  EXF_REQUIRE(tokens >= 0, "%s: tokens must be >= 0", name);
+  EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
+  EXF_REQUIRE(experts >= 1, "%s: experts must be >= 1", name);
+  EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported token id dtype", name);
+  EXF_REQUIRE(table_rows >= 1, "%s: the hash table needs at least one row", name);
+  if (scoring == EXF_SOFTMAX)
+    return fail(EXF_ERR_UNSUPPORTED, "%s: hash routing takes sigmoid or sqrtsoftplus scores", name);
+  EXF_REQUIRE(scoring == EXF_SIGMOID || scoring == EXF_SQRTSOFTPLUS, "%s: unknown scoring %d",
+              name, scoring);
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(logits && token_ids && table && out_w && out_ids, "%s: null pointer", name);
+  return cuda_status(launch_router_hash(logits, tokens, experts, top_k, scoring, token_ids,
+                                        id_dtype, table, table_rows, renormalize, scaling, out_w,
+                                        out_ids, (cudaStream_t)stream),
+                     name);
 }
 
 EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int layers, int experts,

@@ -73,8 +73,47 @@ __device__ __forceinline__ float approx_sigmoid(float x) {
   x = fminf(x, 88.0f);
   return __fdividef(1.0f, 1.0f + __expf(-x));
 }
-// Bound on |approx_sigmoid(x) + b - (exact_sigmoid(x) + b)| with a wide safety factor.
+// sqrt(softplus(x)), the "sqrtsoftplus" router score: softplus(x) = max(x, 0) + log1p(exp(-|x|))
+// with exact_exp (NaN goes to its lower clamp), log1p(y) for 0 < y <= 1 as 2 atanh(u), u =
+// y / (2 + y) <= 1/3: 2u (1 + u^2/3 + ... + u^14/15) by Horner in u^2 with fused multiply-adds
+// (truncation below 2e-9 relative), then the IEEE square root.
+__device__ __forceinline__ float exact_log1p_unit(float y) {
+  const float u = __fdiv_rn(y, __fadd_rn(2.0f, y));
+  const float s = __fmul_rn(u, u);
+  float q = 0x1.111112p-4f;           // 1/15
+  q = __fmaf_rn(q, s, 0x1.3b13b2p-4f);  // 1/13
+  q = __fmaf_rn(q, s, 0x1.745d18p-4f);  // 1/11
+  q = __fmaf_rn(q, s, 0x1.c71c72p-4f);  // 1/9
+  q = __fmaf_rn(q, s, 0x1.24924ap-3f);  // 1/7
+  q = __fmaf_rn(q, s, 0x1.99999ap-3f);  // 1/5
+  q = __fmaf_rn(q, s, 0x1.555556p-2f);  // 1/3
+  q = __fmaf_rn(q, s, 1.0f);
+  return __fmul_rn(__fmul_rn(2.0f, u), q);
+}
+__device__ __forceinline__ float exact_sqrtsoftplus(float x) {
+  const float e = exact_exp(-fabsf(x));
+  return __fsqrt_rn(__fadd_rn(fmaxf(x, 0.0f), exact_log1p_unit(e)));
+}
+// Fast version for candidate preselection; NaN is mapped as in the exact version.
+__device__ __forceinline__ float approx_sqrtsoftplus(float x) {
+  float t = -fabsf(x);
+  t = t > -87.0f ? t : -87.0f;
+  return sqrtf(fmaxf(x, 0.0f) + __logf(1.0f + __expf(t)));
+}
+
+// Bound on |approx score + b - (exact score + b)| (sigmoid and sqrtsoftplus) with a wide safety
+// factor.
 constexpr float kSigmoidMargin = 1.0e-4f;
+
+// The biased-score routers: EXF_SIGMOID or EXF_SQRTSOFTPLUS.
+template <int SCORING>
+__device__ __forceinline__ float exact_score(float x) {
+  return SCORING == EXF_SQRTSOFTPLUS ? exact_sqrtsoftplus(x) : exact_sigmoid(x);
+}
+template <int SCORING>
+__device__ __forceinline__ float approx_score(float x) {
+  return SCORING == EXF_SQRTSOFTPLUS ? approx_sqrtsoftplus(x) : approx_sigmoid(x);
+}
 
 // Keys: floats mapped to unsigned ints in IEEE 754 totalOrder (-NaN < -inf < ... < -0 < +0 <
 // ... < +inf < +NaN), two instructions.  key_of additionally ranks -0 equal to +0, which is

@@ -74,6 +74,10 @@ struct AlignParams {
 };
 
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p, cudaStream_t s);
+cudaError_t launch_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
+                               int scoring, const void* token_ids, int id_dtype,
+                               const int32_t* table, int64_t table_rows, int renormalize,
+                               float scaling, float* out_w, int32_t* out_ids, cudaStream_t s);
 // One token per thread, bulk-copied tiles: 128 experts, softmax, top-8, renormalised, Qwen3 fold
 // or none, 16-byte aligned logits and outputs.
 bool router_tpt_eligible(int experts, int scoring, int fold, const RouterParams& p);

@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
 
   for (int64_t base = gt - g; base < total; base += stride, gt += stride) {
     const bool valid = gt < total;
-    const float* brow = (SCORING == EXF_SIGMOID && p.bias) ? p.bias + layer * E : nullptr;
+    const float* brow = (SCORING != EXF_SOFTMAX && p.bias) ? p.bias + layer * E : nullptr;
 
     // ---- stage, selection keys (IEEE total order; exact logits or fast sigmoid) -------------
     uint32_t keys[32];
@@ -131,13 +131,13 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
       const float4 v = nv[i];
       *reinterpret_cast<float4*>(sv + col) = v;
       float x[4] = {v.x, v.y, v.z, v.w};
-      if (SCORING == EXF_SIGMOID) {
+      if (SCORING != EXF_SOFTMAX) {
         const float4 b = brow ? __ldg(reinterpret_cast<const float4*>(brow + col))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        x[0] = approx_sigmoid(x[0]) + b.x;
-        x[1] = approx_sigmoid(x[1]) + b.y;
-        x[2] = approx_sigmoid(x[2]) + b.z;
-        x[3] = approx_sigmoid(x[3]) + b.w;
+        x[0] = approx_score<SCORING>(x[0]) + b.x;
+        x[1] = approx_score<SCORING>(x[1]) + b.y;
+        x[2] = approx_score<SCORING>(x[2]) + b.z;
+        x[3] = approx_score<SCORING>(x[3]) + b.w;
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) keys[4 * i + c] = order_key(x[c]);
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
 #pragma unroll
     for (int i = 1; i < 8; ++i)
       if (i == K - 1) theta = top[i];
-    if (SCORING == EXF_SIGMOID)
+    if (SCORING != EXF_SOFTMAX)
       theta = order_key(float_of_key(theta) - 2.0f * kSigmoidMargin);
     else if (theta == kKeyPosZero)
       theta = kKeyNegZero;  // -0 ranks equal to +0
@@ -205,8 +205,8 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
         const float x = sv[col];
         float val;
         uint32_t k;
-        if (SCORING == EXF_SIGMOID) {
-          val = exact_sigmoid(x);
+        if (SCORING != EXF_SOFTMAX) {
+          val = exact_score<SCORING>(x);
           k = key_of(__fadd_rn(val, brow ? __ldg(brow + col) : 0.0f));
         } else {
           val = x;
@@ -240,8 +240,8 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
           const int col = 4 * (r + L * (j >> 2)) + (j & 3);
           const float x = sv[col];
           const uint32_t k =
-              (SCORING == EXF_SIGMOID)
-                  ? key_of(__fadd_rn(exact_sigmoid(x), brow ? __ldg(brow + col) : 0.0f))
+              (SCORING != EXF_SOFTMAX)
+                  ? key_of(__fadd_rn(exact_score<SCORING>(x), brow ? __ldg(brow + col) : 0.0f))
                   : key_of(x);
           const unsigned long long pk =
               ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)col);
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
         if (r == 0) {
           const int col = (int)(0xFFFFFFFFu - (uint32_t)best);
           sidx[s] = col;
-          sval[s] = (SCORING == EXF_SIGMOID) ? exact_sigmoid(sv[col]) : sv[col];
+          sval[s] = (SCORING != EXF_SOFTMAX) ? exact_score<SCORING>(sv[col]) : sv[col];
         }
       }
     }
@@ -285,10 +285,12 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
       }
 #pragma unroll
       for (int q = 0; q < L; ++q) norm = __fadd_rn(norm, __shfl_sync(0xffffffffu, part, q, L));
-    } else if (SCORING == EXF_SIGMOID && !p.renormalize) {
+    } else if (SCORING != EXF_SOFTMAX && !p.renormalize) {
       divide = false;
     } else {
       for (int s = 0; s < K; ++s) norm = __fadd_rn(norm, swt[s]);
+      // sqrtsoftplus clamps the divisor (vLLM fused_topk_bias: sum.clamp(min=1e-20))
+      if (SCORING == EXF_SQRTSOFTPLUS && norm < 1.0e-20f) norm = 1.0e-20f;
     }
     if (valid) {
       for (int s = r; s < K; s += L) {
@@ -590,6 +592,87 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Hash routing (DeepSeek-V4 hash-MoE layers; vLLM fused_topk_bias with hash_indices_table, called
+// from exfold/deepseek_v4/vllm_patch.py:175-209): the routes of token t are table[token_ids[t]],
+// in table order; their weights are the unbiased scores of those experts, renormalised (the
+// sqrtsoftplus divisor clamped at 1e-20) and scaled.  One thread per token.  A token id outside
+// the table gives ids -1 and weights 0; a table entry outside [0, experts) keeps its id and
+// gets weight 0, so nothing is read out of range.
+template <int SCORING, typename TID>
+__global__ void __launch_bounds__(256) router_hash_kernel(
+    const float* logits, int64_t tokens, int E, int K, const TID* token_ids, const int32_t* table,
+    int64_t rows, int renormalize, float scaling, float* out_w, int32_t* out_ids) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= tokens) return;
+  const int64_t tid = (int64_t)token_ids[t];
+  float* ow = out_w + t * K;
+  int32_t* oi = out_ids + t * K;
+  if (tid < 0 || tid >= rows) {
+    for (int s = 0; s < K; ++s) {
+      ow[s] = 0.0f;
+      oi[s] = -1;
+    }
+    return;
+  }
+  const int32_t* trow = table + tid * K;
+  const float* xrow = logits + t * E;
+  float w[kMaxK];
+  int id[kMaxK];
+  float sum = 0.0f;
+#pragma unroll
+  for (int s = 0; s < kMaxK; ++s) {
+    if (s < K) {
+      const int e = __ldg(trow + s);
+      id[s] = e;
+      w[s] = (e >= 0 && e < E) ? exact_score<SCORING>(__ldg(xrow + e)) : 0.0f;
+      sum = __fadd_rn(sum, w[s]);
+    }
+  }
+  if (SCORING == EXF_SQRTSOFTPLUS && sum < 1.0e-20f) sum = 1.0e-20f;
+#pragma unroll
+  for (int s = 0; s < kMaxK; ++s) {
+    if (s < K) {
+      float x = renormalize ? __fdiv_rn(w[s], sum) : w[s];
+      if (scaling != 1.0f) x = __fmul_rn(x, scaling);
+      ow[s] = x;
+      oi[s] = id[s];
+    }
+  }
+}
+
+template <int SCORING, typename TID>
+static cudaError_t launch_hash_t(const float* logits, int64_t tokens, int E, int K,
+                                 const void* token_ids, const int32_t* table, int64_t rows,
+                                 int renormalize, float scaling, float* out_w, int32_t* out_ids,
+                                 cudaStream_t stream) {
+  const unsigned blocks = (unsigned)((tokens + 255) / 256);
+  router_hash_kernel<SCORING, TID><<<blocks, 256, 0, stream>>>(
+      logits, tokens, E, K, static_cast<const TID*>(token_ids), table, rows, renormalize, scaling,
+      out_w, out_ids);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
+                               int scoring, const void* token_ids, int id_dtype,
+                               const int32_t* table, int64_t table_rows, int renormalize,
+                               float scaling, float* out_w, int32_t* out_ids, cudaStream_t s) {
+  const bool i32 = id_dtype == EXF_I32;
+  if (scoring == EXF_SQRTSOFTPLUS)
+    return i32 ? launch_hash_t<EXF_SQRTSOFTPLUS, int32_t>(logits, tokens, experts, top_k, token_ids,
+                                                          table, table_rows, renormalize, scaling,
+                                                          out_w, out_ids, s)
+               : launch_hash_t<EXF_SQRTSOFTPLUS, int64_t>(logits, tokens, experts, top_k, token_ids,
+                                                          table, table_rows, renormalize, scaling,
+                                                          out_w, out_ids, s);
+  return i32 ? launch_hash_t<EXF_SIGMOID, int32_t>(logits, tokens, experts, top_k, token_ids, table,
+                                                   table_rows, renormalize, scaling, out_w,
+                                                   out_ids, s)
+             : launch_hash_t<EXF_SIGMOID, int64_t>(logits, tokens, experts, top_k, token_ids, table,
+                                                   table_rows, renormalize, scaling, out_w,
+                                                   out_ids, s);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Host launchers
 template <int E, int SCORING, int FOLD>
 static cudaError_t launch_router_e(const RouterParams& p, cudaStream_t stream) {
@@ -623,6 +706,11 @@ cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams
     if (fold == kFoldNone) return launch_router_s<EXF_SOFTMAX, kFoldNone>(experts, p, stream);
     if (fold == kFoldQwen3) return launch_router_s<EXF_SOFTMAX, kFoldQwen3>(experts, p, stream);
     return launch_router_s<EXF_SOFTMAX, kFoldDsv4>(experts, p, stream);
+  }
+  if (scoring == EXF_SQRTSOFTPLUS) {
+    if (fold == kFoldNone) return launch_router_s<EXF_SQRTSOFTPLUS, kFoldNone>(experts, p, stream);
+    if (fold == kFoldQwen3) return launch_router_s<EXF_SQRTSOFTPLUS, kFoldQwen3>(experts, p, stream);
+    return launch_router_s<EXF_SQRTSOFTPLUS, kFoldDsv4>(experts, p, stream);
   }
   if (fold == kFoldNone) return launch_router_s<EXF_SIGMOID, kFoldNone>(experts, p, stream);
   if (fold == kFoldQwen3) return launch_router_s<EXF_SIGMOID, kFoldQwen3>(experts, p, stream);

@@ -17,7 +17,7 @@ DEFAULT_PATH = Path(__file__).resolve().parent.parent / "lib" / "libexfold_b200.
 EXF_OK, EXF_ERR_INVALID, EXF_ERR_UNSUPPORTED, EXF_ERR_CUDA = 0, -1, -2, -3
 EXF_F32, EXF_BF16, EXF_F16 = 0, 1, 2
 EXF_I32, EXF_I64 = 0, 1
-EXF_SOFTMAX, EXF_SIGMOID = 0, 1
+EXF_SOFTMAX, EXF_SIGMOID, EXF_SQRTSOFTPLUS = 0, 1, 2
 EXF_QWEN3, EXF_DSV4 = 0, 1
 
 _vp, _i, _i64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
@@ -29,6 +29,7 @@ SIGNATURES = {
     "exf_router_topk": (_i, [_vp, _i64, _i, _i, _i, _vp, _i, _f, _vp, _vp, _vp]),
     "exf_router_fold_prefill": (_i, [_vp, _i64, _i, _i, _i, _i, _vp, _i, _f, _i, _i, _i, _vp, _vp,
                                      _vp, _vp, _vp, _vp]),
+    "exf_router_hash": (_i, [_vp, _i64, _i, _i, _i, _vp, _i, _vp, _i64, _i, _f, _vp, _vp, _vp]),
     "exf_fold_prefill": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
                               _vp]),
     "exf_decode": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

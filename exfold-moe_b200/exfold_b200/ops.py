@@ -16,7 +16,7 @@ from . import _lib as L
 
 _WDT = {torch.float32: L.EXF_F32, torch.bfloat16: L.EXF_BF16, torch.float16: L.EXF_F16}
 _IDT = {torch.int32: L.EXF_I32, torch.int64: L.EXF_I64}
-_SCORING = {"softmax": L.EXF_SOFTMAX, "sigmoid": L.EXF_SIGMOID}
+_SCORING = {"softmax": L.EXF_SOFTMAX, "sigmoid": L.EXF_SIGMOID, "sqrtsoftplus": L.EXF_SQRTSOFTPLUS}
 _VARIANT = {"qwen3": L.EXF_QWEN3, "dsv4": L.EXF_DSV4}
 
 
@@ -75,6 +75,30 @@ def router_topk(logits: torch.Tensor, top_k: int, scoring: str = "softmax",
     L.check(L.lib().exf_router_topk(x.data_ptr(), tokens, experts, top_k, _SCORING[scoring],
                                     _ptr(b), int(renormalize), float(scaling), w.data_ptr(),
                                     ids.data_ptr(), _stream(dev)))
+    return w, ids
+
+
+def router_hash(logits: torch.Tensor, token_ids: torch.Tensor, table: torch.Tensor,
+                scoring: str = "sqrtsoftplus", renormalize: bool = True,
+                scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Hash routing: routes table[token_ids] (table [rows, top_k], in table order) weighted by
+    the unbiased scores of those experts -> (weights fp32, ids int32) [tokens, top_k]."""
+    dev = _require_cuda(logits, token_ids, table)
+    x = _f32c(logits)
+    tokens, experts = x.shape
+    tid = _ids_in(token_ids.reshape(-1))
+    if tid.numel() != tokens:
+        raise ValueError(f"token_ids has {tid.numel()} entries for {tokens} tokens")
+    tab = table.to(torch.int32).contiguous()
+    if tab.dim() != 2:
+        raise ValueError("table must be [rows, top_k]")
+    top_k = tab.shape[1]
+    w = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
+    ids = torch.empty((tokens, top_k), dtype=torch.int32, device=dev)
+    L.check(L.lib().exf_router_hash(x.data_ptr(), tokens, experts, top_k, _SCORING[scoring],
+                                    tid.data_ptr(), _IDT[tid.dtype], tab.data_ptr(), tab.shape[0],
+                                    int(renormalize), float(scaling), w.data_ptr(), ids.data_ptr(),
+                                    _stream(dev)))
     return w, ids
 
 

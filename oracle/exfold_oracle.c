@@ -56,6 +56,31 @@ ORC_API float orc_sigmoid(float x) {
   return 1.0f / (1.0f + e);
 }
 
+/* sqrt(softplus(x)), the "sqrtsoftplus" router score of vLLM's fused_topk_bias
+ * (vllm fused_topk_bias_router.py: F.softplus(gating_output).sqrt()), used by
+ * exfold/deepseek_v4/vllm_patch.py:175-209 through module.scoring_func.
+ * softplus(x) = max(x, 0) + log1p(exp(-|x|)) with the exp above (NaN maps to
+ * its lower clamp, so softplus(NaN) = log1p(e^-87)); log1p(y), 0 < y <= 1, as
+ * 2 atanh(u) with u = y / (2 + y) <= 1/3: 2u (1 + u^2/3 + u^4/5 + ... + u^14/15)
+ * by Horner in u^2 with fused multiply-adds (truncation below 2e-9 relative);
+ * then the IEEE square root. */
+static const float kInvOdd[8] = {1.0f,           0x1.555556p-2f, 0x1.99999ap-3f, 0x1.24924ap-3f,
+                                 0x1.c71c72p-4f, 0x1.745d18p-4f, 0x1.3b13b2p-4f, 0x1.111112p-4f};
+ORC_API float orc_log1p_unit(float y) {
+  const float u = y / (2.0f + y);
+  const float s = u * u;
+  float p = kInvOdd[7];
+  for (int i = 6; i >= 0; --i) p = fmaf(p, s, kInvOdd[i]);
+  return (2.0f * u) * p;
+}
+ORC_API float orc_sqrtsoftplus(float x) {
+  const float e = orc_exp(-fabsf(x));
+  return sqrtf(fmaxf(x, 0.0f) + orc_log1p_unit(e));
+}
+static inline float orc_score(int scoring, float x) {
+  return scoring == 1 ? orc_sigmoid(x) : orc_sqrtsoftplus(x);
+}
+
 /* Total order on float keys: IEEE 754 totalOrder (a NaN ranks by its sign bit: above +inf
  * when clear, below -inf when set), except that -0 ranks equal to +0. */
 ORC_API uint32_t orc_key(float x) {
@@ -90,7 +115,7 @@ ORC_API void orc_router_topk(const float* logits, int64_t tokens, int experts, i
     const float* x = logits + t * experts;
     for (int e = 0; e < experts; ++e) {
       float k = x[e];
-      if (scoring == 1) k = orc_sigmoid(x[e]) + (bias ? bias[e] : 0.0f);
+      if (scoring != 0) k = orc_score(scoring, x[e]) + (bias ? bias[e] : 0.0f);
       keys[e] = orc_key(k);
       taken[e] = 0;
     }
@@ -120,9 +145,12 @@ ORC_API void orc_router_topk(const float* logits, int64_t tokens, int experts, i
     } else {
       float sum = 0.0f;
       for (int s = 0; s < top_k; ++s) {
-        w[s] = orc_sigmoid(x[ids[s]]);
+        w[s] = orc_score(scoring, x[ids[s]]);
         sum = sum + w[s];
       }
+      /* sqrtsoftplus clamps the divisor at 1e-20 (vllm fused_topk_bias_router.py
+       * _topk_softplus_sqrt_torch: sum.clamp(min=1e-20)) */
+      if (scoring == 2 && sum < 1e-20f) sum = 1e-20f;
       if (renormalize)
         for (int s = 0; s < top_k; ++s) w[s] = w[s] / sum;
     }
@@ -131,6 +159,45 @@ ORC_API void orc_router_topk(const float* logits, int64_t tokens, int experts, i
   }
   free(keys);
   free(taken);
+}
+
+/* ------------------------------------------------------------------------- */
+/* Hash routing (DeepSeek-V4 hash-MoE layers): vllm fused_topk_bias_router.py
+ * (hash_indices_table[input_tokens], weights = the unbiased scores gathered at
+ * those ids, renormalised, times the scaling factor), called by
+ * exfold/deepseek_v4/vllm_patch.py:175-209 with module.gate.tid2eid.  Routes
+ * keep the table's order.  scoring 1 = sigmoid, 2 = sqrtsoftplus.  A token id
+ * outside the table gives ids -1 and weights 0; a table entry outside
+ * [0, experts) keeps its id and gets weight 0 (both would index out of range
+ * in the reference). */
+ORC_API void orc_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
+                             int scoring, const int64_t* token_ids, const int32_t* table,
+                             int64_t table_rows, int renormalize, float scaling,
+                             float* out_w, int32_t* out_ids) {
+  for (int64_t t = 0; t < tokens; ++t) {
+    float* w = out_w + t * top_k;
+    int32_t* ids = out_ids + t * top_k;
+    const int64_t tid = token_ids[t];
+    if (tid < 0 || tid >= table_rows) {
+      for (int s = 0; s < top_k; ++s) {
+        ids[s] = -1;
+        w[s] = 0.0f;
+      }
+      continue;
+    }
+    float sum = 0.0f;
+    for (int s = 0; s < top_k; ++s) {
+      const int32_t e = table[tid * top_k + s];
+      ids[s] = e;
+      w[s] = (e >= 0 && e < experts) ? orc_score(scoring, logits[t * experts + e]) : 0.0f;
+      sum = sum + w[s];
+    }
+    if (scoring == 2 && sum < 1e-20f) sum = 1e-20f;
+    if (renormalize)
+      for (int s = 0; s < top_k; ++s) w[s] = w[s] / sum;
+    if (scaling != 1.0f)
+      for (int s = 0; s < top_k; ++s) w[s] = w[s] * scaling;
+  }
 }
 
 /* ------------------------------------------------------------------------- */

@@ -32,6 +32,9 @@ def _load() -> ctypes.CDLL:
     sig = {
         "orc_exp": (_c.c_float, [_c.c_float]),
         "orc_sigmoid": (_c.c_float, [_c.c_float]),
+        "orc_sqrtsoftplus": (_c.c_float, [_c.c_float]),
+        "orc_router_hash": (None, [_f32p, _c.c_int64, _c.c_int, _c.c_int, _c.c_int, _i64p, _i32p,
+                                   _c.c_int64, _c.c_int, _c.c_float, _f32p, _i32p]),
         "orc_key": (_c.c_uint32, [_c.c_float]),
         "orc_fixed_point": (_c.c_int64, [_c.c_float]),
         "orc_router_topk": (None, [_f32p, _c.c_int64, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p,
@@ -81,7 +84,7 @@ def _i32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.int32)
 
 
-SCORING = {"softmax": 0, "sigmoid": 1}
+SCORING = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 
 
 def router_topk(logits, top_k: int, scoring: str = "softmax", bias=None,
@@ -95,6 +98,28 @@ def router_topk(logits, top_k: int, scoring: str = "softmax", bias=None,
                           None if b is None else b.ctypes.data, int(renormalize),
                           float(scaling), w, ids)
     return w, ids
+
+
+def router_hash(logits, token_ids, table, scoring: str = "sqrtsoftplus", renormalize: bool = True,
+                scaling: float = 1.0):
+    """Hash routing: ids = table[token_ids] (table [rows, top_k]), weights = the unbiased
+    scores at those ids."""
+    x = _f32(logits)
+    tokens, experts = x.shape
+    tab = _i32(table)
+    top_k = tab.shape[1]
+    tid = np.ascontiguousarray(token_ids, dtype=np.int64)
+    w = np.empty((tokens, top_k), np.float32)
+    ids = np.empty((tokens, top_k), np.int32)
+    lib().orc_router_hash(x, tokens, experts, top_k, SCORING[scoring], tid, tab, tab.shape[0],
+                          int(renormalize), float(scaling), w, ids)
+    return w, ids
+
+
+def sqrtsoftplus(x):
+    f = lib().orc_sqrtsoftplus
+    return np.array([f(float(v)) for v in np.asarray(x, np.float32).ravel()], np.float32).reshape(
+        np.shape(x))
 
 
 def fold_qwen3(w, ids, coeff, loss, target_k: int):

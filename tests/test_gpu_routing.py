@@ -143,6 +143,78 @@ def test_router_sigmoid_e256_ties_and_options():
             np.testing.assert_array_equal(host(w), ew)
 
 
+@pytest.mark.parametrize("experts", [64, 128, 256, 512])
+def test_router_sqrtsoftplus_matches_oracle(experts):
+    """DeepSeek-V4 sqrtsoftplus scoring (vLLM fused_topk_bias scoring_func="sqrtsoftplus"):
+    exact keys sqrt(softplus(x)) + bias, with and without a bias, renormalised or not; logits
+    include quantised rows, extremes and NaN."""
+    x = W.logits(505 + experts, 2077, experts) * 3
+    x[500:900] = np.round(x[500:900] * 4) / 4
+    x[901, 3] = 95.0
+    x[902, 5] = -120.0
+    x[903, 7] = np.nan
+    x[904] = -90.0
+    bias = W.router_bias(505, experts)
+    for b in (bias, None):
+        for k, renorm, scaling in ((8, True, 1.0), (6, False, 2.5)):
+            w, ids = ops.router_topk(cuda(x), k, "sqrtsoftplus", None if b is None else cuda(b),
+                                     renormalize=renorm, scaling=scaling)
+            ew, ei = O.router_topk(x, k, "sqrtsoftplus", b, renorm, scaling)
+            np.testing.assert_array_equal(host(ids), ei)
+            np.testing.assert_array_equal(host(w), ew)
+
+
+def test_router_fold_sqrtsoftplus_dsv4_and_qwen3():
+    lay = W.layer("dsv4_prefill", tokens=4101)
+    coeff, loss, conf = dsv4_tables(lay)
+    for mode in (0, 1, 2):
+        w, ids = ops.router_fold_prefill(cuda(lay.logits), 8, 3, cuda(coeff), cuda(loss),
+                                         scoring="sqrtsoftplus", bias=cuda(lay.bias),
+                                         variant="dsv4", renorm_mode=mode, conf_loss=cuda(conf))
+        ew, ei = O.router_fold(lay.logits, 8, 3, coeff, loss, scoring="sqrtsoftplus",
+                               bias=lay.bias, variant="dsv4", conf_loss=conf, renorm_mode=mode)
+        np.testing.assert_array_equal(host(ids), ei)
+        np.testing.assert_array_equal(host(w), ew)
+    w, ids = ops.router_fold_prefill(cuda(lay.logits), 8, 4, cuda(coeff), cuda(loss),
+                                     scoring="sqrtsoftplus", bias=cuda(lay.bias))
+    ew, ei = O.router_fold(lay.logits, 8, 4, coeff, loss, scoring="sqrtsoftplus", bias=lay.bias)
+    np.testing.assert_array_equal(host(ids), ei)
+    np.testing.assert_array_equal(host(w), ew)
+
+
+@pytest.mark.parametrize("id_dtype", [torch.int32, torch.int64])
+def test_router_hash_matches_oracle(id_dtype):
+    """Hash-MoE routing (tid2eid[input_ids]): table order kept, unbiased scores as weights;
+    out-of-range token ids and table entries read nothing out of range."""
+    rng = np.random.default_rng(6)
+    x = W.logits(606, 3001, 256)
+    table = np.stack([rng.choice(256, 8, replace=False) for _ in range(5000)]).astype(np.int32)
+    table[7, 3] = 300
+    table[8, 0] = -2
+    tok = rng.integers(0, 5000, 3001).astype(np.int64)
+    tok[:20] = np.arange(20)
+    tok[20], tok[21] = -1, 5000
+    for scoring in ("sqrtsoftplus", "sigmoid"):
+        for renorm, scaling in ((True, 1.0), (False, 2.5)):
+            w, ids = ops.router_hash(cuda(x), cuda(tok).to(id_dtype), cuda(table), scoring,
+                                     renorm, scaling)
+            ew, ei = O.router_hash(x, tok, table, scoring, renorm, scaling)
+            np.testing.assert_array_equal(host(ids), ei)
+            np.testing.assert_array_equal(host(w), ew)
+    # the DeepSeek-V4 fold of hash routes (weights sorted inside the fold)
+    w, ids = ops.router_hash(cuda(x), cuda(tok), cuda(table), "sqrtsoftplus")
+    lay = W.layer("dsv4_prefill", tokens=64)
+    coeff, loss, conf = dsv4_tables(lay)
+    valid = (host(ids) >= 0).all(1) & (host(ids) < 256).all(1)
+    fw, fi = ops.fold_prefill(w[cuda(valid)], ids[cuda(valid)], cuda(coeff), cuda(loss), 3,
+                              variant="dsv4", renorm_mode=2, conf_loss=cuda(conf))
+    efw, efi = O.fold_dsv4(host(w)[valid], host(ids)[valid], coeff, loss, conf, 3, 2)
+    np.testing.assert_array_equal(host(fi), efi)
+    np.testing.assert_array_equal(host(fw), efw)
+    with pytest.raises(NotImplementedError):
+        ops.router_hash(cuda(x), cuda(tok), cuda(table), "softmax")
+
+
 def test_router_ties_constant_rows_and_specials():
     """Exact ties take the lower expert id; constant rows, +-inf and NaN stay in range."""
     x = W.logits(5, 256, 128)
