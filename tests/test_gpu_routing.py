@@ -215,6 +215,24 @@ def test_router_hash_matches_oracle(id_dtype):
         ops.router_hash(cuda(x), cuda(tok), cuda(table), "softmax")
 
 
+def test_native_route_is_router_or_hash():
+    from exfold_b200.deepseek_v4.routing import native_route
+
+    x = W.logits(707, 1000, 256)
+    bias = W.router_bias(707, 256)
+    table = np.stack([np.roll(np.arange(256), i)[:8] for i in range(50)]).astype(np.int32)
+    tok = np.arange(1000) % 50
+    w, ids = native_route(cuda(x), 8, "sqrtsoftplus", cuda(bias), True, 2.0)
+    ew, ei = O.router_topk(x, 8, "sqrtsoftplus", bias, True, 2.0)
+    np.testing.assert_array_equal(host(ids), ei)
+    np.testing.assert_array_equal(host(w), ew)
+    w, ids = native_route(cuda(x), 8, "sigmoid", cuda(bias), True, 1.0, input_ids=cuda(tok),
+                          tid2eid=cuda(table))
+    ew, ei = O.router_hash(x, tok, table, "sigmoid", True, 1.0)
+    np.testing.assert_array_equal(host(ids), ei)
+    np.testing.assert_array_equal(host(w), ew)
+
+
 def test_router_ties_constant_rows_and_specials():
     """Exact ties take the lower expert id; constant rows, +-inf and NaN stay in range."""
     x = W.logits(5, 256, 128)

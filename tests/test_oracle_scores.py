@@ -101,3 +101,13 @@ def test_max_projection_loss_threshold(monkeypatch):
     monkeypatch.delenv("EXFOLD_MAX_PROJECTION_LOSS")
     dl = calibration.prepare_dsv4({k: v.clone() for k, v in payload.items()})[4]
     assert torch.equal(dl[off], src[off])
+
+
+def test_native_route_requires_input_ids_for_hash_layers():
+    import pytest
+
+    from exfold_b200.deepseek_v4.routing import native_route
+
+    with pytest.raises(RuntimeError, match="requires input_ids"):
+        native_route(torch.zeros(2, 256), 8, "sqrtsoftplus",
+                     tid2eid=torch.zeros(10, 8, dtype=torch.int32))
