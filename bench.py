@@ -515,6 +515,21 @@ def run_extra(args) -> None:
         nbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
         out.update(tokens=lay.tokens, us_per_launch=ms * 1e3, tokens_per_s=lay.tokens / ms * 1e3,
                    gbs=nbytes / ms / 1e6, hbm_frac_of_measured_peak=nbytes / ms / 1e6 / peaks["hbm_gbs"])
+    elif args.workload == "calibration_update":
+        # PairwiseScalarStats.update (exfold/qwen3/calibration.py:49-95) at the Qwen3 layer shape:
+        # 8 routes of 2048-wide bf16 expert outputs over 128 experts, 16384 tokens per call
+        # (512 MiB of outputs > L2); the pass is bound by reading the outputs.
+        from exfold_b200.calibration import PairwiseScalarStats
+
+        T, K, H, E = (args.tokens or 16384), 8, 2048, 128
+        outs = torch.randn((T, K, H), generator=gen, device=dev).to(torch.bfloat16)
+        ids = torch.randint(0, E, (T, K), generator=gen, device=dev, dtype=torch.int32)
+        stats = PairwiseScalarStats(E, device=dev)
+        ms = _timed_graph(lambda: stats.update(ids, outs), steps, max(3, args.warmup), dev)
+        nbytes = T * K * H * 2 + T * K * 4
+        out.update(tokens=T, top_k=K, hidden=H, experts=E, us_per_call=ms * 1e3,
+                   tokens_per_s=T / ms * 1e3, gbs=nbytes / ms / 1e6,
+                   hbm_frac_of_measured_peak=nbytes / ms / 1e6 / peaks["hbm_gbs"])
     elif args.workload == "dsv4_decode":
         cfg = W.WORKLOADS["dsv4_decode"]
         rows = []
@@ -547,7 +562,7 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=0, help="fewer experts (profiling cases)")
     ap.add_argument("--workload", default="qwen3_layers",
                     choices=["qwen3_layers", "moe_dsv4_prefill", "moe_qwen3_decode",
-                             "dsv4_prefill_fold", "dsv4_decode"])
+                             "dsv4_prefill_fold", "dsv4_decode", "calibration_update"])
     args = ap.parse_args()
     set_shape(args.layers, args.tokens or TOKENS)
     if args.warmup < 3:

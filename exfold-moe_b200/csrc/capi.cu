@@ -380,4 +380,49 @@ EXF_API int exf_moe_align_noalloc(const void* ids, int id_dtype, int64_t numel, 
   return cuda_status(launch_align_static(id_dtype, p, (cudaStream_t)stream), name);
 }
 
+// ---- calibration statistics (offline) ------------------------------------------------------
+EXF_API int exf_calibration_update(const void* outputs, int out_dtype, const void* ids,
+                                   int id_dtype, int64_t tokens, int top_k, int hidden,
+                                   int experts, double* dot, double* target_sq,
+                                   double* source_sq, double* norm_sum, double* norm_count,
+                                   exf_stream_t stream) {
+  const char* name = "exf_calibration_update";
+  EXF_REQUIRE(good_wdtype(out_dtype) && good_idtype(id_dtype), "%s: unsupported dtype", name);
+  EXF_REQUIRE(tokens >= 0, "%s: tokens must be >= 0", name);
+  EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
+  EXF_REQUIRE(hidden >= 8 && hidden % 8 == 0, "%s: hidden must be a positive multiple of 8", name);
+  EXF_REQUIRE(experts >= 2 && experts <= 1024, "%s: experts must be in [2, 1024]", name);
+  if (tokens == 0) return EXF_OK;
+  EXF_REQUIRE(outputs && ids && dot && target_sq && source_sq && norm_sum && norm_count,
+              "%s: null pointer", name);
+  EXF_REQUIRE(aligned16(outputs), "%s: outputs must be 16-byte aligned", name);
+  return cuda_status(launch_calib_update(out_dtype, id_dtype, outputs, ids, tokens, top_k, hidden,
+                                         experts, dot, target_sq, source_sq, norm_sum, norm_count,
+                                         (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int exf_calibration_finalize(const double* dot, const double* target_sq,
+                                     const double* source_sq, int experts, double ridge,
+                                     double clip_min, double clip_max, float* coeff, float* loss,
+                                     int32_t* nonfinite, exf_stream_t stream) {
+  const char* name = "exf_calibration_finalize";
+  EXF_REQUIRE(experts >= 2 && experts <= 1024, "%s: experts must be in [2, 1024]", name);
+  EXF_REQUIRE(ridge > 0, "%s: ridge must be positive", name);
+  EXF_REQUIRE(clip_min < clip_max, "%s: clip_min must be smaller than clip_max", name);
+  EXF_REQUIRE(dot && target_sq && source_sq && coeff && loss, "%s: null pointer", name);
+  return cuda_status(launch_calib_finalize(dot, target_sq, source_sq, experts, ridge, clip_min,
+                                           clip_max, coeff, loss, nonfinite, (cudaStream_t)stream),
+                     name);
+}
+
+EXF_API int exf_calibration_norms(const double* norm_sum, const double* norm_count, int experts,
+                                  float* norms, exf_stream_t stream) {
+  const char* name = "exf_calibration_norms";
+  EXF_REQUIRE(experts >= 2 && experts <= 1024, "%s: experts must be in [2, 1024]", name);
+  EXF_REQUIRE(norm_sum && norm_count && norms, "%s: null pointer", name);
+  return cuda_status(launch_calib_norms(norm_sum, norm_count, experts, norms, (cudaStream_t)stream),
+                     name);
+}
+
 }  // extern "C"

@@ -93,6 +93,14 @@ cudaError_t launch_static_remap(int w_dtype, int id_dtype, void* w, void* ids, i
                                 int experts, const int32_t* target, const float* scale,
                                 cudaStream_t s);
 cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s);
+cudaError_t launch_calib_update(int out_dtype, int id_dtype, const void* out, const void* ids,
+                                int64_t tokens, int K, int H, int E, double* dot, double* tsq,
+                                double* ssq, double* nsum, double* ncnt, cudaStream_t s);
+cudaError_t launch_calib_finalize(const double* dot, const double* tsq, const double* ssq, int E,
+                                  double ridge, double lo, double hi, float* coeff, float* loss,
+                                  int32_t* nonfinite, cudaStream_t s);
+cudaError_t launch_calib_norms(const double* nsum, const double* ncnt, int E, float* norms,
+                               cudaStream_t s);
 int64_t align_workspace_bytes(int64_t numel, int experts);
 int align_max_experts();
 int64_t align_static_table_ints();

@@ -30,6 +30,11 @@ SIGNATURES = {
     "exf_router_fold_prefill": (_i, [_vp, _i64, _i, _i, _i, _i, _vp, _i, _f, _i, _i, _i, _vp, _vp,
                                      _vp, _vp, _vp, _vp]),
     "exf_router_hash": (_i, [_vp, _i64, _i, _i, _i, _vp, _i, _vp, _i64, _i, _f, _vp, _vp, _vp]),
+    "exf_calibration_update": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                                    _vp]),
+    "exf_calibration_finalize": (_i, [_vp, _vp, _vp, _i, ctypes.c_double, ctypes.c_double,
+                                      ctypes.c_double, _vp, _vp, _vp, _vp]),
+    "exf_calibration_norms": (_i, [_vp, _vp, _i, _vp, _vp]),
     "exf_fold_prefill": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
                               _vp]),
     "exf_decode": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -9,6 +9,8 @@ values:
 * prepare_dsv4: exfold/deepseek_v4/vllm_patch.py:82-170 (key fallbacks; EXFOLD_MAX_PROJECTION_LOSS
   masking of the decode loss; diagonal fixes; norms clamped to float32 eps).
 * DeviceTables: the per-device copy cache of vllm_patch.py:146-157 / 236-260.
+* PairwiseScalarStats: the accumulator that builds the tables (exfold/qwen3/calibration.py:9-140)
+  on the GPU kernels exf_calibration_update / _finalize / _norms.
 
 Arrays may be numpy arrays or torch tensors; the result has the input's kind.
 """
@@ -111,3 +113,95 @@ class DeviceTables:
             cached = tuple(t.to(device=device, non_blocking=True) for t in self._host)
             self._cache[device] = cached
         return cached
+
+
+class PairwiseScalarStats(torch.nn.Module):
+    """One MoE layer's directed scalar projectors, accumulated on the GPU: the drop-in for
+    PairwiseScalarStats (exfold/qwen3/calibration.py:9-140) with the same constructor, buffers
+    (dot, target_sq_norm, source_sq_norm, expert_norm_sum, expert_norm_count; fp64) and methods.
+    update / finalize / expert_norms run the exf_calibration_* kernels; the inputs of update must
+    be CUDA tensors (RuntimeError otherwise, as the reference's CUDA paths raise).  finalize reads
+    back the kernel's non-finite flag (a host synchronisation, like the reference's isfinite
+    checks)."""
+
+    default_loss = _SENTINEL
+
+    def __init__(self, num_experts: int, ridge: float = 1e-3, clip_min: float = -4.0,
+                 clip_max: float = 4.0, device=None) -> None:
+        super().__init__()
+        if num_experts <= 1:
+            raise ValueError("num_experts must be greater than one")
+        if ridge <= 0:
+            raise ValueError("ridge must be positive")
+        if clip_min >= clip_max:
+            raise ValueError("clip_min must be smaller than clip_max")
+        if num_experts > 1024:
+            raise ValueError("num_experts must be at most 1024")
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        shape = (num_experts, num_experts)
+        for name, shp in (("dot", shape), ("target_sq_norm", shape), ("source_sq_norm", shape),
+                          ("expert_norm_sum", (num_experts,)),
+                          ("expert_norm_count", (num_experts,))):
+            self.register_buffer(name, torch.zeros(shp, dtype=torch.float64, device=dev),
+                                 persistent=False)
+        self.num_experts = num_experts
+        self.ridge = ridge
+        self.clip_min = clip_min
+        self.clip_max = clip_max
+
+    @torch.no_grad()
+    def update(self, expert_ids: torch.Tensor, expert_outputs: torch.Tensor) -> None:
+        """Accumulate co-routed expert outputs: expert_ids [tokens, top_k], expert_outputs
+        [tokens, top_k, hidden] (unweighted; fp32, bf16 or fp16)."""
+        from . import _lib as L
+        from .ops import _IDT, _WDT, _stream
+
+        if expert_ids.ndim != 2:
+            raise ValueError("expert_ids must have shape [tokens, top_k]")
+        if expert_outputs.shape[:2] != expert_ids.shape or expert_outputs.ndim != 3:
+            raise ValueError("expert_outputs must have shape [tokens, top_k, hidden_size]")
+        if not (expert_ids.is_cuda and expert_outputs.is_cuda):
+            raise RuntimeError("PairwiseScalarStats.update expects CUDA tensors")
+        out = expert_outputs if expert_outputs.dtype in _WDT else expert_outputs.float()
+        out = out.contiguous()
+        if out.data_ptr() % 16:
+            out = out.clone()
+        ids = expert_ids if expert_ids.dtype in _IDT else expert_ids.to(torch.int64)
+        ids = ids.contiguous()
+        tokens, top_k, hidden = out.shape
+        L.check(L.lib().exf_calibration_update(
+            out.data_ptr(), _WDT[out.dtype], ids.data_ptr(), _IDT[ids.dtype], tokens, top_k,
+            hidden, self.num_experts, self.dot.data_ptr(), self.target_sq_norm.data_ptr(),
+            self.source_sq_norm.data_ptr(), self.expert_norm_sum.data_ptr(),
+            self.expert_norm_count.data_ptr(), _stream(out.device)))
+
+    @torch.no_grad()
+    def finalize(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Return the clipped scalar matrix and relative projection loss (fp32 [E, E])."""
+        from . import _lib as L
+        from .ops import _stream
+
+        E, dev = self.num_experts, self.dot.device
+        coeff = torch.empty((E, E), dtype=torch.float32, device=dev)
+        loss = torch.empty((E, E), dtype=torch.float32, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        L.check(L.lib().exf_calibration_finalize(
+            self.dot.data_ptr(), self.target_sq_norm.data_ptr(), self.source_sq_norm.data_ptr(), E,
+            float(self.ridge), float(self.clip_min), float(self.clip_max), coeff.data_ptr(),
+            loss.data_ptr(), flag.data_ptr(), _stream(dev)))
+        if int(flag.item()):
+            raise RuntimeError("non-finite calibration statistics")
+        return coeff, loss
+
+    @torch.no_grad()
+    def expert_norms(self) -> torch.Tensor:
+        """Return the mean output norm of each routed expert (fp32 [E])."""
+        from . import _lib as L
+        from .ops import _stream
+
+        dev = self.expert_norm_sum.device
+        norms = torch.empty(self.num_experts, dtype=torch.float32, device=dev)
+        L.check(L.lib().exf_calibration_norms(self.expert_norm_sum.data_ptr(),
+                                              self.expert_norm_count.data_ptr(), self.num_experts,
+                                              norms.data_ptr(), _stream(dev)))
+        return norms

@@ -183,6 +183,35 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
                               int experts, int hidden, int inter, void* y, void* workspace,
                               int64_t workspace_bytes, int32_t* status, exf_stream_t stream);
 
+/* Calibration statistics (offline): the GPU form of PairwiseScalarStats
+ * (exfold/qwen3/calibration.py:9-140), which builds the [E][E] coefficient / loss tables and the
+ * expert norms that the folds above read.
+ * exf_calibration_update (PairwiseScalarStats.update, calibration.py:49-95): outputs
+ * [tokens][top_k][hidden] unweighted expert outputs (out_dtype; 16-byte aligned, hidden a
+ * multiple of 8), ids [tokens][top_k].  For each token and ordered pair of its routes with
+ * different experts (s, d), with w_s = ||u_s||, adds w_s <u_s, u_d>, w_s ||u_d||^2 and
+ * w_s ||u_s||^2 (each formed in fp32) to dot, target_sq, source_sq at [e_s][e_d] (fp64 [E][E],
+ * caller-zeroed at the start of a calibration); adds ||u|| and 1 to norm_sum, norm_count [E]
+ * for every route.  Routes with an expert id outside [0, experts) are skipped.  Accumulation is
+ * by fp64 atomics, so the low bits depend on their order, as with the reference's index_add_.
+ * exf_calibration_finalize (finalize, calibration.py:97-126): coeff, loss fp32 [E][E]; sets
+ * *nonfinite (device int32, may be NULL) to 1 when a statistic is not finite (the reference
+ * raises RuntimeError; the caller reads the flag).
+ * exf_calibration_norms (expert_norms, calibration.py:128-140): norms fp32 [E], the mean output
+ * norm of each routed expert, the lower median of those for the others (1 when none was routed).
+ * 2 <= experts <= 1024; 1 <= top_k <= 8. */
+EXF_API int exf_calibration_update(const void* outputs, int out_dtype, const void* ids,
+                                   int id_dtype, int64_t tokens, int top_k, int hidden,
+                                   int experts, double* dot, double* target_sq,
+                                   double* source_sq, double* norm_sum, double* norm_count,
+                                   exf_stream_t stream);
+EXF_API int exf_calibration_finalize(const double* dot, const double* target_sq,
+                                     const double* source_sq, int experts, double ridge,
+                                     double clip_min, double clip_max, float* coeff, float* loss,
+                                     int32_t* nonfinite, exf_stream_t stream);
+EXF_API int exf_calibration_norms(const double* norm_sum, const double* norm_count, int experts,
+                                  float* norms, exf_stream_t stream);
+
 /* exf_moe_align for callers that cannot allocate device memory at call time.  This entry point
  * has no counterpart in the reference.
  *

@@ -3,9 +3,9 @@
 Run in a container that has the reference project checked out (read-only)
 at REFERENCE_ROOT (default /root/reference):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [calibration]
 
-The reference's Triton kernels (exfold/qwen3/kernels.py) run on CPU tensors
+(with `calibration`, only calibration_reference.npz is written).  The reference's Triton kernels (exfold/qwen3/kernels.py) run on CPU tensors
 under TRITON_INTERPRET=1, launched exactly as their host wrappers launch them
 (the wrappers themselves refuse CPU tensors).  The DeepSeek-V4 CUDA kernels
 cannot run without a GPU, so the DeepSeek-V4 fixtures come from the
@@ -297,7 +297,37 @@ def workload_cases():
     return out
 
 
+def calibration_cases():
+    """The reference accumulator (exfold/qwen3/calibration.py PairwiseScalarStats) on CPU:
+    random routes with duplicate expert ids and experts that are never routed (median fallback
+    of expert_norms), outputs rounded to bf16 so the same values can be fed in bf16."""
+    from exfold.qwen3.calibration import PairwiseScalarStats
+
+    out = {}
+    gen = torch.Generator().manual_seed(9001)
+    for name, (E, T, k, H, hi) in {"a": (16, 300, 8, 96, 12), "b": (24, 64, 6, 520, 24)}.items():
+        ids = torch.randint(0, hi, (T, k), generator=gen)
+        outputs = torch.randn((T, k, H), generator=gen).bfloat16().float()
+        stats = PairwiseScalarStats(E, ridge=1e-3, clip_min=-4.0, clip_max=4.0)
+        half = T // 2
+        stats.update(ids[:half], outputs[:half])
+        stats.update(ids[half:], outputs[half:])
+        coeff, loss = stats.finalize()
+        out.update({f"{name}_ids": n(ids).astype(np.int32), f"{name}_outputs": n(outputs),
+                    f"{name}_dot": n(stats.dot), f"{name}_target_sq": n(stats.target_sq_norm),
+                    f"{name}_source_sq": n(stats.source_sq_norm),
+                    f"{name}_norm_sum": n(stats.expert_norm_sum),
+                    f"{name}_norm_count": n(stats.expert_norm_count),
+                    f"{name}_coeff": n(coeff), f"{name}_loss": n(loss),
+                    f"{name}_norms": n(stats.expert_norms())})
+    return out
+
+
 def main():
+    if sys.argv[1:] == ["calibration"]:
+        np.savez_compressed(HERE / "calibration_reference.npz", **calibration_cases())
+        return
+    np.savez_compressed(HERE / "calibration_reference.npz", **calibration_cases())
     np.savez_compressed(HERE / "qwen3_reference_tests.npz", **qwen3_tests())
     np.savez_compressed(HERE / "dsv4_reference_tests.npz", **dsv4_tests())
     np.savez_compressed(HERE / "qwen3_artifact_layers.npz", **artifact_layers())
