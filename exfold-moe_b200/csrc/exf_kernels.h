@@ -82,6 +82,10 @@ cudaError_t launch_router_hash(const float* logits, int64_t tokens, int experts,
 // or none, 16-byte aligned logits and outputs.
 bool router_tpt_eligible(int experts, int scoring, int fold, const RouterParams& p);
 cudaError_t launch_router_tpt(int fold, const RouterParams& p, cudaStream_t s);
+// Two lanes per token, bulk-copied tiles: 256 experts, biased sigmoid, top-8, DeepSeek-V4 fold or
+// none, 16-byte aligned logits (and outputs without a fold, selection loss with one).
+bool router_biased_eligible(int experts, int scoring, int fold, const RouterParams& p);
+cudaError_t launch_router_biased(int fold, const RouterParams& p, cudaStream_t s);
 cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p, cudaStream_t s);
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,

@@ -702,6 +702,8 @@ static cudaError_t launch_router_s(int experts, const RouterParams& p, cudaStrea
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p,
                           cudaStream_t stream) {
   if (router_tpt_eligible(experts, scoring, fold, p)) return launch_router_tpt(fold, p, stream);
+  if (router_biased_eligible(experts, scoring, fold, p))
+    return launch_router_biased(fold, p, stream);
   if (scoring == EXF_SOFTMAX) {
     if (fold == kFoldNone) return launch_router_s<EXF_SOFTMAX, kFoldNone>(experts, p, stream);
     if (fold == kFoldQwen3) return launch_router_s<EXF_SOFTMAX, kFoldQwen3>(experts, p, stream);
