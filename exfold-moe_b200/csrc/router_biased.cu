@@ -245,13 +245,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
     } else {
       *failed = 1;
     }
-    p9 = 0;
-    p10 = 0;
-#pragma unroll
-    for (int q = 0; q < kK; ++q) pk[q] = 0;
+    // approximate group maxima, keyed: the only reads of the tile
+    uint32_t g[32];
     if (ok) {
       const float* rowp = sm.tile[slot] + rowi * kE;
-      uint32_t g[32];
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
@@ -264,6 +261,22 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
           const uint32_t id = (static_cast<uint32_t>(h) << 5) | (8 * s + i);
           g[8 * s + i] = (order_key(m) & ~63u) | (63u - id);
         }
+    }
+    // the tile is consumed: refill its slot with local tile k + kSlots before the sorting
+    // network (generic-proxy reads of the slot are ordered before the bulk copy that overwrites
+    // it)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (t == 0 && ok && k + kSlots < nk) {
+      issue(k + kSlots);
+      __threadfence_block();
+      seq[slot] = k + kSlots;
+    }
+    p9 = 0;
+    p10 = 0;
+#pragma unroll
+    for (int q = 0; q < kK; ++q) pk[q] = 0;
+    if (ok) {
       sort8<uint32_t, cx32>(g);
       sort8<uint32_t, cx32>(g + 8);
       sort8<uint32_t, cx32>(g + 16);
@@ -284,15 +297,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       p10 = max(p10, o10);
 #pragma unroll
       for (int q = 0; q < kK; ++q) pk[q] = g[q];
-    }
-    // the tile is consumed: refill its slot with local tile k + kSlots (generic-proxy reads of
-    // the slot are ordered before the bulk copy that overwrites it)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    if (t == 0 && ok && k + kSlots < nk) {
-      issue(k + kSlots);
-      __threadfence_block();
-      seq[slot] = k + kSlots;
     }
     return ok;
   };
