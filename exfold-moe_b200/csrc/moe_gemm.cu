@@ -177,19 +177,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Tiles t = m_block * n_tiles + n_tile, strided over the persistent CTAs: the N tiles of one
-  // block run side by side (A and the expert's weights are reused from L2).  Blocks past the
-  // padded route count, or of no expert, are skipped by every role alike.
-  const int post = *p.num_post_pad;
-  const int m_used = (post + kBM - 1) / kBM < p.m_blocks ? (post + kBM - 1) / kBM : p.m_blocks;
-  const int ntiles = m_used * p.n_tiles;
-  auto tile_expert = [&](int t, int& m_block, int& n_tile) {
-    m_block = t / p.n_tiles;
-    n_tile = t - m_block * p.n_tiles;
-    const int e = p.expert_ids[m_block];
-    return (e >= 0 && e < p.experts) ? e : -1;
-  };
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -207,6 +194,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  // Launched as a programmatic dependent: the set-up above overlaps the previous kernel's tail;
+  // nothing it wrote is read before this wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // Tiles t = m_block * n_tiles + n_tile, strided over the persistent CTAs: the N tiles of one
+  // block run side by side (A and the expert's weights are reused from L2).  Blocks past the
+  // padded route count, or of no expert, are skipped by every role alike.
+  const int post = *p.num_post_pad;
+  const int m_used = (post + kBM - 1) / kBM < p.m_blocks ? (post + kBM - 1) / kBM : p.m_blocks;
+  const int ntiles = m_used * p.n_tiles;
+  auto tile_expert = [&](int t, int& m_block, int& n_tile) {
+    m_block = t / p.n_tiles;
+    n_tile = t - m_block * p.n_tiles;
+    const int e = p.expert_ids[m_block];
+    return (e >= 0 && e < p.experts) ? e : -1;
+  };
   const uint32_t tmem = sm.tmem_base;
   volatile int* failed = &sm.failed;
   const int kblocks = p.k / kBK;
@@ -352,25 +356,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---- gather and combine ---------------------------------------------------------------------
-// xs[m] = x[sorted_ids[m] / top_k] for real routes, zero rows for padding (16-byte vectors).
+// xs[m] = x[sorted_ids[m] / top_k] for the real routes of the used rows (16-byte vectors).
+// Padding rows keep whatever the workspace holds: the GEMM rows are independent, GEMM-1's
+// padding rows only feed GEMM-2's padding rows, and those are never stored.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* x,
                                                           const int32_t* sorted_ids,
                                                           const int32_t* num_post_pad,
                                                           int64_t rows, int numel, int top_k,
                                                           int hidden, __nv_bfloat16* xs) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int vec = hidden / 8;
-  const int post = *num_post_pad;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * vec;
+  const int64_t used = *num_post_pad < rows ? *num_post_pad : rows;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < used * vec;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / vec;
     const int c = (int)(i - m * vec);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (m < post) {
-      const int route = sorted_ids[m];
-      if (route < numel)
-        v = reinterpret_cast<const uint4*>(x + (int64_t)(route / top_k) * hidden)[c];
-    }
-    reinterpret_cast<uint4*>(xs + m * hidden)[c] = v;
+    const int route = sorted_ids[m];
+    if (route < numel)
+      reinterpret_cast<uint4*>(xs + m * hidden)[c] =
+          reinterpret_cast<const uint4*>(x + (int64_t)(route / top_k) * hidden)[c];
   }
 }
 
@@ -380,6 +385,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* out,
                                                       const int32_t* ids, int experts,
                                                       int64_t tokens, int top_k, int hidden,
                                                       __nv_bfloat16* y) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int vec = hidden / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tokens * vec;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -460,6 +467,25 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Launch as a programmatic dependent of the previous kernel in the stream (the kernel calls
+// griddepcontrol.wait before reading anything that kernel wrote).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 // One CTA per SM (192 KB of pipeline stages and all 512 TMEM columns), never more than tiles.
 static unsigned persistent_tiles(const ExpertGemmParams& p) {
   const int64_t tiles = (int64_t)p.m_blocks * p.n_tiles;
@@ -517,10 +543,10 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
     int64_t blocks = (work + 255) / 256;
     const int lim = 8 * sm_count();
     if (lim > 0 && blocks > lim) blocks = lim;
-    gather_rows_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(a.x), w.sorted_ids, w.num_post_pad, cap, (int)numel,
-        a.top_k, a.hidden, w.xs);
-    e = cudaGetLastError();
+    e = launch_pdl(gather_rows_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
+                   static_cast<const __nv_bfloat16*>(a.x), static_cast<const int32_t*>(w.sorted_ids),
+                   static_cast<const int32_t*>(w.num_post_pad), cap, (int)numel, a.top_k, a.hidden,
+                   w.xs);
     if (e != cudaSuccess) return e;
   }
   // 3. GEMM-1 + SwiGLU
@@ -541,8 +567,8 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
   p.act = w.act;
   p.m_blocks = (int)(cap / kBM);
   p.n_tiles = a.inter / (kBN / 2);
-  expert_gemm_kernel<kGemmSwiGLU><<<persistent_tiles(p), kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
-  e = cudaGetLastError();
+  e = launch_pdl(expert_gemm_kernel<kGemmSwiGLU>, persistent_tiles(p), kGemmThreads,
+                 kGemmSmemBytes, s, ma, mb, p);
   if (e != cudaSuccess) return e;
   // 4. GEMM-2, weighted per-route rows
   if (!make_map(&ma, w.act, cap, a.inter, kBM) ||
@@ -553,8 +579,8 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
   p.route_w = a.topk_w;
   p.out = w.out;
   p.n_tiles = a.hidden / kBN;
-  expert_gemm_kernel<kGemmDown><<<persistent_tiles(p), kGemmThreads, kGemmSmemBytes, s>>>(ma, mb, p);
-  e = cudaGetLastError();
+  e = launch_pdl(expert_gemm_kernel<kGemmDown>, persistent_tiles(p), kGemmThreads,
+                 kGemmSmemBytes, s, ma, mb, p);
   if (e != cudaSuccess) return e;
   // 5. combine the routes of each token
   {
@@ -562,11 +588,10 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
     int64_t blocks = (work + 255) / 256;
     const int lim = 8 * sm_count();
     if (lim > 0 && blocks > lim) blocks = lim;
-    combine_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, s>>>(
-        w.out, a.topk_ids, a.experts, a.tokens, a.top_k, a.hidden,
-        static_cast<__nv_bfloat16*>(a.y));
+    return launch_pdl(combine_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
+                      static_cast<const __nv_bfloat16*>(w.out), a.topk_ids, a.experts, a.tokens,
+                      a.top_k, a.hidden, static_cast<__nv_bfloat16*>(a.y));
   }
-  return cudaGetLastError();
 }
 
 }  // namespace exf
