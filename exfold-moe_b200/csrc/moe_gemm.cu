@@ -1,17 +1,18 @@
 // Grouped SwiGLU expert GEMMs on the 5th-generation tensor cores (sm_100a: tcgen05 + TMA).
 //
 // After moe_align, routes are grouped by expert and padded to 128-row blocks.  Per MoE layer:
-//   gather : xs[m] = x[token(sorted_ids[m])]                      (bf16 rows; padding rows = 0)
+//   gather : xs[m] = x[token(sorted_ids[m])]                      (bf16 rows of real routes)
 //   GEMM-1 : act[m, n] = silu(xs[m] . W1[e, n]) * (xs[m] . W3[e, n]) for n in a 128-wide tile;
 //            gate and up rows of W13[e] are stacked into one N = 256 MMA so both accumulators
 //            sit side by side in TMEM and the SwiGLU epilogue needs no second pass
 //   GEMM-2 : out[route, h] = w_route * (act[m] . W2[e, h])         (N = 256 tile of H)
 //   combine: y[t, h] = sum over the token's routes of out[route, h] (fixed order: deterministic)
 //
-// Both GEMMs share one mainloop in a persistent kernel: one CTA per SM walks 128 x 256 output
-// tiles (one expert each); warp 0 streams 128 x 64 A and 256 x 64 B bf16 tiles with TMA
-// (128-byte swizzle) through a 4-stage mbarrier ring that runs on across tiles; one elected
-// thread of warp 1 issues tcgen05.mma (M = 128, N = 256, K = 16, fp32 accumulation in TMEM) and
+// Both GEMMs share one mainloop in a persistent kernel: one CTA per SM walks 128 x BN output
+// tiles (one expert each; BN = 256, or 128 when the experts hold few routes, as at decode);
+// warp 0 streams 128 x 64 A and BN x 64 B bf16 tiles with TMA (128-byte swizzle) through a
+// 4-stage (6 at BN = 128) mbarrier ring that runs on across tiles; one elected
+// thread of warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16, fp32 accumulation in TMEM) and
 // releases each stage with tcgen05.commit; warps 2-5 read the accumulator with tcgen05.ld and run
 // the epilogue.  Two TMEM accumulators (all 512 columns) let the epilogue of one tile overlap
 // the mainloop of the next.  The N tiles of one M block run side by side on neighbouring CTAs,
@@ -30,27 +31,38 @@
 namespace exf {
 
 constexpr int kBM = 128;              // rows per M block (moe_align block size)
-constexpr int kBN = 256;              // MMA N
 constexpr int kBK = 64;               // bf16 elements per 128-byte swizzled row
-constexpr int kStages = 4;
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
-constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kGemmThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kTmemCols = 512;       // two 256-column fp32 accumulators
+constexpr int kTmemCols = 512;       // two accumulators of up to 256 fp32 columns
 constexpr uint32_t kWaitLimit = 1u << 20;
 
+// The MMA N tile: 256 for prefill; 128 when experts hold few routes (decode), which doubles the
+// tiles over the same weight bytes (2.6 -> 5.2 tiles per CTA at the Qwen3 decode shape, so the
+// last round idles fewer SMs) with 6 stages of 32 KB instead of 4 of 48 KB.
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kBTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  // instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M=128, N=BN
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                     ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+};
+
+template <int BN>
 struct GemmSmem {
-  alignas(1024) uint8_t tiles[kStages][kStageBytes];
-  alignas(8) uint64_t full[kStages];
-  alignas(8) uint64_t empty[kStages];
+  alignas(1024) uint8_t tiles[GemmCfg<BN>::kStages][GemmCfg<BN>::kStageBytes];
+  alignas(8) uint64_t full[GemmCfg<BN>::kStages];
+  alignas(8) uint64_t empty[GemmCfg<BN>::kStages];
   alignas(8) uint64_t acc_full[2];   // accumulator b holds a finished tile
   alignas(8) uint64_t acc_empty[2];  // the epilogue has read accumulator b
   alignas(8) uint64_t drain;         // every MMA issued by the CTA has completed
   uint32_t tmem_base;
   int failed;
 };
-constexpr size_t kGemmSmemBytes = sizeof(GemmSmem) + 1024;  // + alignment slack
+template <int BN>
+constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem<BN>) + 1024; }  // + alignment slack
 
 // ---- PTX helpers ------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -124,16 +136,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M=128, N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
-
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -167,12 +176,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // ---- the shared mainloop + per-GEMM epilogue ------------------------------------------------
 enum GemmKind { kGemmSwiGLU = 0, kGemmDown = 1 };
 
-template <int KIND>
+template <int KIND, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, const ExpertGemmParams p) {
+  constexpr int kBN = BN;
+  constexpr int kStages = GemmCfg<BN>::kStages;
+  constexpr int kBTileBytes = GemmCfg<BN>::kBTileBytes;
+  constexpr int kStageBytes = GemmCfg<BN>::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+  GemmSmem<BN>& sm = *reinterpret_cast<GemmSmem<BN>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -271,7 +284,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             mma_bf16(acc, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
-                     (kb > 0 || k > 0) ? 1u : 0u);
+                     GemmCfg<BN>::kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
           mma_commit(&sm.empty[s]);
         }
         if (!ok) break;
@@ -444,13 +457,18 @@ static cudaError_t allow_gemm_smem() {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (done[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemBytes);
-  if (e == cudaSuccess) done[dev] = true;
-  return e;
+  const int s256 = (int)gemm_smem_bytes<256>(), s128 = (int)gemm_smem_bytes<128>();
+  if ((e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 256>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown, 256>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 128>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, s128)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown, 128>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, s128)) != cudaSuccess)
+    return e;
+  done[dev] = true;
+  return cudaSuccess;
 }
 
 // 2-D bf16 tensor [rows][cols] (row-major, cols contiguous) read in box_rows x 64 tiles.
@@ -527,6 +545,44 @@ MoeWorkspace moe_workspace(int64_t tokens, int top_k, int experts, int hidden, i
   return w;
 }
 
+// GEMM-1 (+ SwiGLU) and GEMM-2 of launch_moe_experts with an N tile of BN.
+template <int BN>
+static cudaError_t launch_gemms(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+  const int64_t numel = a.tokens * a.top_k;
+  const int64_t cap = w.capacity;
+  constexpr size_t smem = gemm_smem_bytes<BN>();
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, w.xs, cap, a.hidden, kBM) ||
+      !make_map(&mb, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, BN / 2))
+    return cudaErrorInvalidValue;
+  ExpertGemmParams p{};
+  p.num_post_pad = w.num_post_pad;
+  p.expert_ids = w.expert_ids;
+  p.sorted_ids = w.sorted_ids;
+  p.experts = a.experts;
+  p.numel = (int)numel;
+  p.hidden = a.hidden;
+  p.status = a.status;
+  p.k = a.hidden;
+  p.n_total = a.inter;
+  p.act = w.act;
+  p.m_blocks = (int)(cap / kBM);
+  p.n_tiles = a.inter / (BN / 2);
+  cudaError_t e = launch_pdl(expert_gemm_kernel<kGemmSwiGLU, BN>, persistent_tiles(p),
+                             kGemmThreads, smem, s, ma, mb, p);
+  if (e != cudaSuccess) return e;
+  if (!make_map(&ma, w.act, cap, a.inter, kBM) ||
+      !make_map(&mb, a.w2, (uint64_t)a.experts * a.hidden, a.inter, BN))
+    return cudaErrorInvalidValue;
+  p.k = a.inter;
+  p.n_total = a.hidden;
+  p.route_w = a.topk_w;
+  p.out = w.out;
+  p.n_tiles = a.hidden / BN;
+  return launch_pdl(expert_gemm_kernel<kGemmDown, BN>, persistent_tiles(p), kGemmThreads, smem,
+                    s, ma, mb, p);
+}
+
 cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
   const int64_t numel = a.tokens * a.top_k;
   const int64_t cap = w.capacity;
@@ -549,38 +605,9 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
                    w.xs);
     if (e != cudaSuccess) return e;
   }
-  // 3. GEMM-1 + SwiGLU
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, w.xs, cap, a.hidden, kBM) ||
-      !make_map(&mb, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, kBN / 2))
-    return cudaErrorInvalidValue;
-  ExpertGemmParams p{};
-  p.num_post_pad = w.num_post_pad;
-  p.expert_ids = w.expert_ids;
-  p.sorted_ids = w.sorted_ids;
-  p.experts = a.experts;
-  p.numel = (int)numel;
-  p.hidden = a.hidden;
-  p.status = a.status;
-  p.k = a.hidden;
-  p.n_total = a.inter;
-  p.act = w.act;
-  p.m_blocks = (int)(cap / kBM);
-  p.n_tiles = a.inter / (kBN / 2);
-  e = launch_pdl(expert_gemm_kernel<kGemmSwiGLU>, persistent_tiles(p), kGemmThreads,
-                 kGemmSmemBytes, s, ma, mb, p);
-  if (e != cudaSuccess) return e;
-  // 4. GEMM-2, weighted per-route rows
-  if (!make_map(&ma, w.act, cap, a.inter, kBM) ||
-      !make_map(&mb, a.w2, (uint64_t)a.experts * a.hidden, a.inter, kBN))
-    return cudaErrorInvalidValue;
-  p.k = a.inter;
-  p.n_total = a.hidden;
-  p.route_w = a.topk_w;
-  p.out = w.out;
-  p.n_tiles = a.hidden / kBN;
-  e = launch_pdl(expert_gemm_kernel<kGemmDown>, persistent_tiles(p), kGemmThreads,
-                 kGemmSmemBytes, s, ma, mb, p);
+  // 3-4. GEMM-1 + SwiGLU, GEMM-2 (N tile 128 when the experts hold 64 routes or fewer on
+  // average, as at decode; 256 otherwise)
+  e = numel <= (int64_t)a.experts * 64 ? launch_gemms<128>(a, w, s) : launch_gemms<256>(a, w, s);
   if (e != cudaSuccess) return e;
   // 5. combine the routes of each token
   {
