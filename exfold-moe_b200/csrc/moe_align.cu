@@ -35,35 +35,41 @@ __device__ __forceinline__ int expert_of(const IT* ids, int64_t r, int64_t end, 
   return (e >= 0 && e < E) ? e : -1;
 }
 
-// Stable scatter of routes [start, end): base[e] holds the next slot of expert e.
-template <typename IT>
-__device__ void stable_scatter(const IT* ids, int64_t start, int64_t end, int E, AlignSmem& sm,
-                               int32_t* sorted_ids) {
+// One round of the stable scatter: route r (expert e, -1 for none) of the CTA's 512 consecutive
+// routes goes to base[e] + (routes of expert e before it in the round); base advances.
+__device__ __forceinline__ void scatter_round(int64_t r, int e, int E, AlignSmem& sm,
+                                              int32_t* sorted_ids) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const unsigned lt = (1u << lane) - 1u;
+  for (int x = lane; x < E; x += 32) sm.wcnt[warp][x] = 0;
+  __syncwarp();
+  const unsigned m = __match_any_sync(0xffffffffu, e);
+  const int lane_rank = __popc(m & lt);
+  if (e >= 0 && lane_rank == 0) sm.wcnt[warp][e] = __popc(m);
+  __syncthreads();
+  if (e >= 0) {
+    int prefix = 0;
+    for (int w = 0; w < warp; ++w) prefix += sm.wcnt[w][e];
+    sorted_ids[sm.base[e] + prefix + lane_rank] = (int32_t)r;
+  }
+  __syncthreads();
+  for (int x = tid; x < E; x += kAlignThreads) {
+    int add = 0;
+    for (int w = 0; w < kAlignWarps; ++w) add += sm.wcnt[w][x];
+    sm.base[x] += add;
+  }
+  __syncthreads();
+}
+
+// Stable scatter of routes [start, end): base[e] holds the next slot of expert e.
+template <typename IT>
+__device__ void stable_scatter(const IT* ids, int64_t start, int64_t end, int E, AlignSmem& sm,
+                               int32_t* sorted_ids) {
   for (int64_t s0 = start; s0 < end; s0 += kAlignThreads) {
-    const int64_t r = s0 + tid;
-    const int e = expert_of(ids, r, end, E);
-    for (int x = lane; x < E; x += 32) sm.wcnt[warp][x] = 0;
-    __syncwarp();
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    const int lane_rank = __popc(m & lt);
-    if (e >= 0 && lane_rank == 0) sm.wcnt[warp][e] = __popc(m);
-    __syncthreads();
-    if (e >= 0) {
-      int prefix = 0;
-      for (int w = 0; w < warp; ++w) prefix += sm.wcnt[w][e];
-      sorted_ids[sm.base[e] + prefix + lane_rank] = (int32_t)r;
-    }
-    __syncthreads();
-    for (int x = tid; x < E; x += kAlignThreads) {
-      int add = 0;
-      for (int w = 0; w < kAlignWarps; ++w) add += sm.wcnt[w][x];
-      sm.base[x] += add;
-    }
-    __syncthreads();
+    const int64_t r = s0 + threadIdx.x;
+    scatter_round(r, expert_of(ids, r, end, E), E, sm, sorted_ids);
   }
 }
 
@@ -74,22 +80,37 @@ __device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
   const int E = p.experts;
   const int BM = p.block_size;
   // experts per thread: E <= kAlignMaxExperts == kAlignThreads, so one expert per thread
+  const int lane = tid & 31, warp = tid >> 5;
   const int c = tid < E ? sm.count[tid] : 0;
   const int padded = (c + BM - 1) / BM * BM;
-  sm.scan[tid] = padded;
-  __syncthreads();
-  for (int d = 1; d < kAlignThreads; d <<= 1) {
-    const int v = tid >= d ? sm.scan[tid - d] : 0;
-    __syncthreads();
-    sm.scan[tid] += v;
-    __syncthreads();
+  // inclusive scan of the padded counts: within each warp by shuffles, then over warp totals
+  int v = padded;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
   }
-  if (tid < E) sm.off[tid + 1] = sm.scan[tid];
+  if (lane == 31) sm.scan[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < kAlignWarps ? sm.scan[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, t, d);
+      if (lane >= d) t += o;
+    }
+    if (lane < kAlignWarps) sm.scan[kAlignWarps + lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  if (warp > 0) v += sm.scan[kAlignWarps + warp - 1];
+  if (tid < E) sm.off[tid + 1] = v;
   if (tid == 0) sm.off[0] = 0;
   __syncthreads();
   const int total = sm.off[E];
-  if (tid < E) {
-    for (int q = sm.off[tid] + c; q < sm.off[tid] + padded; ++q) p.sorted_ids[q] = (int32_t)p.numel;
+  // padding slots of each expert, one warp per expert
+  for (int e = warp; e < E; e += kAlignWarps) {
+    const int q0 = sm.off[e] + sm.count[e], q1 = sm.off[e + 1];
+    for (int q = q0 + lane; q < q1; q += 32) p.sorted_ids[q] = (int32_t)p.numel;
   }
   for (int64_t q = total + tid; q < p.capacity; q += kAlignThreads) p.sorted_ids[q] = (int32_t)p.numel;
   const int64_t nblocks = (p.capacity + BM - 1) / BM;
@@ -112,20 +133,28 @@ __device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
 
 template <typename IT>
 __global__ void __launch_bounds__(kAlignThreads, 1) align_small_kernel(const AlignParams p) {
+  constexpr int kPer = static_cast<int>(kAlignSmall / kAlignThreads);
   __shared__ AlignSmem sm;
   const IT* ids = static_cast<const IT*>(p.ids);
   const int tid = threadIdx.x;
+  // every id this thread handles, loaded once (all loads in flight together): route
+  // j * 512 + tid for round j
+  int ex[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) ex[j] = expert_of(ids, (int64_t)j * kAlignThreads + tid, p.numel, p.experts);
   for (int e = tid; e < p.experts; e += kAlignThreads) sm.count[e] = 0;
   __syncthreads();
-  for (int64_t r = tid; r < p.numel; r += kAlignThreads) {
-    const int e = expert_of(ids, r, p.numel, p.experts);
-    if (e >= 0) atomicAdd(&sm.count[e], 1);
-  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (ex[j] >= 0) atomicAdd(&sm.count[ex[j]], 1);
   __syncthreads();
   scan_and_fill(p, sm);
   for (int e = tid; e < p.experts; e += kAlignThreads) sm.base[e] = sm.off[e];
   __syncthreads();
-  stable_scatter(ids, 0, p.numel, p.experts, sm, p.sorted_ids);
+  const int rounds = static_cast<int>((p.numel + kAlignThreads - 1) / kAlignThreads);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (j < rounds) scatter_round((int64_t)j * kAlignThreads + tid, ex[j], p.experts, sm, p.sorted_ids);
 }
 
 template <typename IT>
