@@ -71,6 +71,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   const int tid = threadIdx.x;
   const WT* w = static_cast<const WT*>(p.w);
   const IT* ids = static_cast<const IT*>(p.ids);
+  // launched as a programmatic dependent: nothing the previous kernel wrote is read before this
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- 1. importance ------------------------------------------------------------------------
   const int copies = kHistLongs / E < 32 ? kHistLongs / E : 32;  // >= 2 for E <= 1024
@@ -368,8 +371,17 @@ __global__ void __launch_bounds__(256) static_remap_kernel(void* wv, void* idv, 
 // ---------------------------------------------------------------------------------------------
 template <typename WT, typename IT>
 static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
-  decode_kernel<WT, IT><<<1, kDecodeThreads, 0, s>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<WT, IT>, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s) {

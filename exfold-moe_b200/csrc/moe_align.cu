@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_small_kernel(const Ali
   __shared__ AlignSmem sm;
   const IT* ids = static_cast<const IT*>(p.ids);
   const int tid = threadIdx.x;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // every id this thread handles, loaded once (all loads in flight together): route
   // j * 512 + tid for round j
   int ex[kPer];
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_small_kernel(const Ali
 template <typename IT>
 __global__ void __launch_bounds__(kAlignThreads) align_count_kernel(const AlignParams p) {
   __shared__ int hist[kAlignMaxExperts];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const IT* ids = static_cast<const IT*>(p.ids);
   const int64_t start = (int64_t)blockIdx.x * kAlignChunk;
   const int64_t end = min(start + kAlignChunk, p.numel);
@@ -176,6 +180,8 @@ __global__ void __launch_bounds__(kAlignThreads) align_count_kernel(const AlignP
 
 __global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const AlignParams p) {
   __shared__ AlignSmem sm;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
   const int E = p.experts;
   if (tid < E) {
@@ -198,6 +204,8 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const Alig
 template <typename IT>
 __global__ void __launch_bounds__(kAlignThreads, 1) align_scatter_kernel(const AlignParams p) {
   __shared__ AlignSmem sm;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const IT* ids = static_cast<const IT*>(p.ids);
   for (int e = threadIdx.x; e < p.experts; e += kAlignThreads)
     sm.base[e] = p.table[(int64_t)blockIdx.x * p.experts + e];
@@ -216,17 +224,31 @@ int64_t align_workspace_bytes(int64_t numel, int experts) {
 
 int align_max_experts() { return kAlignMaxExperts; }
 
+// Every align kernel is launched as a programmatic dependent of the kernel before it in the
+// stream (its launch overlaps that kernel's tail; it reads nothing before griddepcontrol.wait).
+static cudaError_t launch_dependent(void (*kern)(AlignParams), unsigned grid, const AlignParams& p,
+                                    cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kAlignThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 template <typename IT>
 static cudaError_t launch_align_t(AlignParams p, cudaStream_t s) {
-  if (p.numel <= kAlignSmall) {
-    align_small_kernel<IT><<<1, kAlignThreads, 0, s>>>(p);
-    return cudaGetLastError();
-  }
+  if (p.numel <= kAlignSmall) return launch_dependent(align_small_kernel<IT>, 1, p, s);
   p.chunks = (p.numel + kAlignChunk - 1) / kAlignChunk;
-  align_count_kernel<IT><<<(unsigned)p.chunks, kAlignThreads, 0, s>>>(p);
-  align_scan_kernel<<<1, kAlignThreads, 0, s>>>(p);
-  align_scatter_kernel<IT><<<(unsigned)p.chunks, kAlignThreads, 0, s>>>(p);
-  return cudaGetLastError();
+  cudaError_t e = launch_dependent(align_count_kernel<IT>, (unsigned)p.chunks, p, s);
+  if (e == cudaSuccess) e = launch_dependent(align_scan_kernel, 1, p, s);
+  if (e == cudaSuccess) e = launch_dependent(align_scatter_kernel<IT>, (unsigned)p.chunks, p, s);
+  return e;
 }
 
 cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s) {
