@@ -11,14 +11,29 @@
 // w_s ||u_s||^2 (w_s = ||u_s||) into the [E, E] statistics, and ||u_s|| and 1 into the
 // per-expert norm sum and count, with 64-bit atomics in L2 (the reference's index_add_).  The
 // pass is bound by reading the outputs; the fp32 dot products take about half that time.
+// calib_gram_kernel, the same update for bf16 / fp16 outputs with k in {1, 2, 4, 8} and a hidden
+// size that is a multiple of 128, on the tensor cores: 128 / k tokens' routes are 128 consecutive
+// rows of the [tokens * k, hidden] outputs, and one tcgen05.mma chain (M = N = 128, K = 16 per
+// instruction, fp32 in TMEM) computes their Gram matrix X X^T, with the same TMA-loaded tile as
+// both operands.  Only the 128 / k diagonal k x k blocks are used (1/16 of the products at k = 8),
+// which the tensor cores still do in less time than the tile takes to arrive from HBM, so the pass
+// runs at the HBM rate instead of being bound by 36 fp32 FMA chains per token.  The products are
+// exact in fp32; each 128-column slice is summed by the tensor core into one of 4 TMEM
+// accumulators in turn, and the slices' sums are added in fp32 with round-to-nearest (the tensor
+// core's own fp32 chains drop low bits, 1.8e-5 of a dot product over 2048 columns).  Warp roles as in moe_gemm.cu:
+// warp 0 streams 16 KB tiles through an 8-stage ring, warp 1 issues the MMAs, warps 2-5 read
+// their 32 rows' k columns from TMEM and add the same fp64 updates as calib_update_kernel.
 // calib_finalize_kernel (calibration.py:97-126): the closed form element by element in fp64,
 // a device flag for non-finite statistics.  calib_norms_kernel (calibration.py:128-140): mean
 // norm per expert, the lower median of the observed experts for the others.
 #include <float.h>
 
+#include <mutex>
+
 #include "exf_common.cuh"
 #include "exf_kernels.h"
 #include "exf_launch.h"
+#include "exf_tc.cuh"
 
 namespace exf {
 
@@ -201,6 +216,201 @@ __global__ void __launch_bounds__(kUpdWarps * 32) calib_update_kernel(
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
+
+// ---- tensor-core Gram pass ----------------------------------------------------------------------
+constexpr int kGramRows = 128;                          // MMA M = N: 128 / k tokens x k routes
+constexpr int kGramBK = 64;                             // 16-bit columns per 128-byte row
+constexpr int kGramStages = 8;
+constexpr int kGramTile = kGramRows * kGramBK * 2;      // 16 KB
+constexpr int kGramThreads = 192;                       // TMA, MMA, 4 epilogue warps
+// The tensor core's fp32 accumulation chains drop low bits (toward zero) as they go: a 2048-long
+// chain lost up to 1.8e-5 of a dot product.  Chains of kGramPartKb k-blocks (K = 128) go to one
+// of kGramSlots TMEM accumulators in turn, and the epilogue adds the partial products of a block
+// in fp32 with round-to-nearest.
+constexpr int kGramPartKb = 2;
+constexpr int kGramSlots = 4;
+constexpr int kGramTmemCols = kGramSlots * kGramRows;   // all 512 columns
+
+struct GramSmem {
+  alignas(1024) uint8_t tiles[kGramStages][kGramTile];
+  alignas(8) uint64_t full[kGramStages];
+  alignas(8) uint64_t empty[kGramStages];
+  alignas(8) uint64_t acc_full[kGramSlots];
+  alignas(8) uint64_t acc_empty[kGramSlots];
+  alignas(8) uint64_t drain;
+  uint32_t tmem_base;
+  int failed;
+};
+constexpr size_t kGramSmemBytes = sizeof(GramSmem) + 1024;  // + alignment slack
+
+template <bool BF16, typename IT, int KT>
+__global__ void __launch_bounds__(kGramThreads, 1) calib_gram_kernel(
+    const __grid_constant__ CUtensorMap map, const IT* ids, int64_t tokens, int H, int E,
+    double* dot, double* tsq, double* ssq, double* nsum, double* ncnt) {
+  using namespace tc;
+  extern __shared__ uint8_t gram_raw[];
+  GramSmem& sm = *reinterpret_cast<GramSmem*>(
+      (reinterpret_cast<uintptr_t>(gram_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t nblocks = (tokens * KT + kGramRows - 1) / kGramRows;
+  const int kblocks = H / kGramBK;
+  const int nparts = kblocks / kGramPartKb;
+  constexpr uint32_t kIdesc = idesc_f16(kGramRows, kGramRows, BF16);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGramStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < kGramSlots; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&sm.drain, 1);
+    sm.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kGramTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* failed = &sm.failed;
+
+  if (warp == 0) {
+    // ---- TMA producer: rows [128 b, 128 b + 128) x columns [64 kb, 64 kb + 64); rows past the
+    // last route read as zeros
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int64_t b = blockIdx.x; b < nblocks && ok; b += gridDim.x)
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kGramStages;
+          ok = mbar_wait(&sm.empty[s], ((g / kGramStages) & 1) ^ 1, failed);
+          if (!ok) break;
+          mbar_expect_tx(&sm.full[s], kGramTile);
+          tma_load_2d(sm.tiles[s], &map, &sm.full[s], kb * kGramBK,
+                      static_cast<int>(b * kGramRows));
+        }
+      for (uint32_t j = g > kGramStages ? g - kGramStages : 0; j < g; ++j)
+        mbar_wait_drain(&sm.full[j % kGramStages], (j / kGramStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: partial u (k-blocks [2 u', 2 u' + 2) of a block) accumulates X X^T over
+    // its 128 columns into TMEM slot u mod 4, columns [128 (u mod 4), +128)
+    if (lane == 0) {
+      uint32_t g = 0, u = 0;
+      bool ok = true;
+      for (int64_t b = blockIdx.x; b < nblocks && ok; b += gridDim.x)
+        for (int pt = 0; pt < nparts && ok; ++pt, ++u) {
+          const int a = u % kGramSlots;
+          ok = mbar_wait(&sm.acc_empty[a], ((u / kGramSlots) & 1) ^ 1, failed);
+          if (!ok) break;
+          fence_after_sync();
+          const uint32_t acc = tmem + static_cast<uint32_t>(a * kGramRows);
+          for (int j = 0; j < kGramPartKb; ++j, ++g) {
+            const int s = g % kGramStages;
+            ok = mbar_wait(&sm.full[s], (g / kGramStages) & 1, failed);
+            if (!ok) break;
+            fence_after_sync();
+            const uint32_t base = smem_addr(sm.tiles[s]);
+#pragma unroll
+            for (int k = 0; k < kGramBK / 16; ++k) {
+              const uint64_t d = smem_desc(base + k * 32);
+              mma_kind_f16(acc, d, d, kIdesc, (j > 0 || k > 0) ? 1u : 0u);
+            }
+            mma_commit(&sm.empty[s]);
+          }
+          if (!ok) break;
+          mma_commit(&sm.acc_full[a]);
+        }
+      mma_commit(&sm.drain);
+      mbar_wait_drain(&sm.drain, 0);
+    }
+  } else {
+    // ---- epilogue: warp q owns TMEM lanes (rows) 32q .. 32q + 31, i.e. 32 / k whole tokens,
+    // whose k columns lie in columns 32q .. 32q + 31
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const int s = r % KT;          // route of the token (128 is a multiple of k)
+    const int gl = lane - s;       // lane of the token's route 0
+    uint32_t u = 0;
+    bool live = true;
+    for (int64_t b = blockIdx.x; b < nblocks && live; b += gridDim.x) {
+      // this row of the token's k x k block: G[s][d] = the sum over the partials of
+      // v[k * (lane / k) + d]
+      float gr[KT];
+#pragma unroll
+      for (int d = 0; d < KT; ++d) gr[d] = 0.0f;
+      for (int pt = 0; pt < nparts; ++pt, ++u) {
+        const int a = u % kGramSlots;
+        const bool ok = mbar_wait(&sm.acc_full[a], (u / kGramSlots) & 1, failed);
+        fence_after_sync();
+        // warp-uniform: the TMEM load below is collective
+        if (!__all_sync(0xffffffffu, ok && !*failed)) {
+          live = false;
+          break;
+        }
+        float v[32];
+        tmem_load32(tmem + static_cast<uint32_t>(a * kGramRows + 32 * q) +
+                        (static_cast<uint32_t>(32 * q) << 16),
+                    v);
+        // the slot has been read: the MMA thread may fill it again
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.acc_empty[a]);
+#pragma unroll
+        for (int d = 0; d < KT; ++d) {
+          float x = v[d];
+#pragma unroll
+          for (int c = 1; c < 32 / KT; ++c)
+            if (lane / KT == c) x = v[c * KT + d];
+          gr[d] = __fadd_rn(gr[d], x);
+        }
+      }
+      if (!live) break;
+      float sq_s = gr[0];
+#pragma unroll
+      for (int d = 1; d < KT; ++d)
+        if (s == d) sq_s = gr[d];
+      const int64_t row = b * kGramRows + r;
+      const int64_t t = row / KT;
+      const bool valid = t < tokens;
+      const int es_raw = valid ? static_cast<int>(ids[row]) : -1;
+      const int es = (es_raw >= 0 && es_raw < E) ? es_raw : -1;
+      const float w = __fsqrt_rn(sq_s);
+      float sq_d[KT];
+      int ed[KT];
+#pragma unroll
+      for (int d = 0; d < KT; ++d) {
+        sq_d[d] = __shfl_sync(0xffffffffu, sq_s, gl + d);
+        ed[d] = __shfl_sync(0xffffffffu, es, gl + d);
+      }
+      if (es < 0) continue;
+      atomicAdd(nsum + es, (double)w);
+      atomicAdd(ncnt + es, 1.0);
+#pragma unroll
+      for (int d = 0; d < KT; ++d) {
+        if (d == s || ed[d] < 0 || ed[d] == es) continue;
+        const int64_t idx = (int64_t)es * E + ed[d];
+        atomicAdd(dot + idx, (double)__fmul_rn(gr[d], w));
+        atomicAdd(tsq + idx, (double)__fmul_rn(sq_d[d], w));
+        atomicAdd(ssq + idx, (double)__fmul_rn(sq_s, w));
+      }
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after_sync();
+    tmem_free(tmem, kGramTmemCols);
+  }
+  // a wait that timed out left statistics out: make them non-finite, which finalize reports
+  if (threadIdx.x == 0 && sm.failed) atomicAdd(dot, __longlong_as_double(0x7FF8000000000000ll));
+}
+
 __global__ void __launch_bounds__(256) calib_finalize_kernel(
     const double* dot, const double* tsq, const double* ssq, int E, double ridge, double lo,
     double hi, float* coeff, float* loss, int32_t* nonfinite) {
@@ -280,6 +490,65 @@ cudaError_t launch_update_t(const void* out, const void* ids, int64_t tokens, in
   return cudaGetLastError();
 }
 
+template <bool BF16, typename IT, int KT>
+cudaError_t launch_gram_k(const CUtensorMap& map, const void* ids, int64_t tokens, int H, int E,
+                          double* dot, double* tsq, double* ssq, double* nsum, double* ncnt,
+                          cudaStream_t s) {
+  auto kern = calib_gram_kernel<BF16, IT, KT>;
+  static std::mutex mu;
+  static bool opted[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!opted[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kGramSmemBytes);
+      if (e != cudaSuccess) return e;
+      opted[dev] = true;
+    }
+  }
+  int64_t blocks = (tokens * KT + kGramRows - 1) / kGramRows;
+  const int sms = sm_count();
+  if (sms > 0 && blocks > sms) blocks = sms;
+  if (blocks < 1) blocks = 1;
+  kern<<<(unsigned)blocks, kGramThreads, kGramSmemBytes, s>>>(
+      map, static_cast<const IT*>(ids), tokens, H, E, dot, tsq, ssq, nsum, ncnt);
+  return cudaGetLastError();
+}
+
+// The tensor-core pass when the shape allows it (bf16 / fp16 outputs, k in {1, 2, 4, 8}, hidden
+// a multiple of 128, rows addressable by 32-bit TMA coordinates); cudaErrorNotSupported otherwise.
+template <bool BF16>
+cudaError_t launch_gram(int id_dtype, const void* out, const void* ids, int64_t tokens, int K,
+                        int H, int E, double* dot, double* tsq, double* ssq, double* nsum,
+                        double* ncnt, cudaStream_t s) {
+  if ((K != 1 && K != 2 && K != 4 && K != 8) || H % (kGramBK * kGramPartKb) != 0 ||
+      tokens * K > (int64_t)0x7FFFFF00)
+    return cudaErrorNotSupported;
+  CUtensorMap map;
+  if (!tc::make_map(&map, out, (uint64_t)tokens * K, (uint64_t)H, kGramRows,
+                    BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
+    return cudaErrorNotSupported;
+  const bool i32 = id_dtype == EXF_I32;
+#define EXF_GRAM_K(KV)                                                                        \
+  case KV:                                                                                    \
+    return i32 ? launch_gram_k<BF16, int32_t, KV>(map, ids, tokens, H, E, dot, tsq, ssq,      \
+                                                  nsum, ncnt, s)                               \
+               : launch_gram_k<BF16, int64_t, KV>(map, ids, tokens, H, E, dot, tsq, ssq,      \
+                                                  nsum, ncnt, s);
+  switch (K) {
+    EXF_GRAM_K(1)
+    EXF_GRAM_K(2)
+    EXF_GRAM_K(4)
+    default:
+      EXF_GRAM_K(8)
+  }
+#undef EXF_GRAM_K
+}
+
 template <typename T>
 cudaError_t launch_update_w(int id_dtype, const void* out, const void* ids, int64_t tokens, int K,
                             int H, int E, double* dot, double* tsq, double* ssq, double* nsum,
@@ -294,6 +563,15 @@ cudaError_t launch_update_w(int id_dtype, const void* out, const void* ids, int6
 cudaError_t launch_calib_update(int out_dtype, int id_dtype, const void* out, const void* ids,
                                 int64_t tokens, int K, int H, int E, double* dot, double* tsq,
                                 double* ssq, double* nsum, double* ncnt, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (out_dtype == EXF_BF16 || out_dtype == EXF_F16) {
+    const cudaError_t e =
+        out_dtype == EXF_BF16
+            ? launch_gram<true>(id_dtype, out, ids, tokens, K, H, E, dot, tsq, ssq, nsum, ncnt, s)
+            : launch_gram<false>(id_dtype, out, ids, tokens, K, H, E, dot, tsq, ssq, nsum, ncnt,
+                                 s);
+    if (e != cudaErrorNotSupported) return e;
+  }
   switch (out_dtype) {
     case EXF_F32:
       return launch_update_w<float>(id_dtype, out, ids, tokens, K, H, E, dot, tsq, ssq, nsum, ncnt, s);

@@ -27,15 +27,16 @@
 #include "exf_common.cuh"
 #include "exf_launch.h"
 #include "exf_moe.h"
+#include "exf_tc.cuh"
 
 namespace exf {
+using namespace tc;
 
 constexpr int kBM = 128;              // rows per M block (moe_align block size)
 constexpr int kBK = 64;               // bf16 elements per 128-byte swizzled row
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kGemmThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTmemCols = 512;       // two accumulators of up to 256 fp32 columns
-constexpr uint32_t kWaitLimit = 1u << 20;
 
 // The MMA N tile: 256 for prefill; 128 when experts hold few routes (decode), which doubles the
 // tiles over the same weight bytes (2.6 -> 5.2 tiles per CTA at the Qwen3 decode shape, so the
@@ -45,9 +46,7 @@ struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : 6;
   static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  // instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M=128, N=BN
-  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
-                                     ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  static constexpr uint32_t kIdesc = idesc_f16(kBM, BN, true);  // bf16, M=128, N=BN
 };
 
 template <int BN>
@@ -63,115 +62,6 @@ struct GemmSmem {
 };
 template <int BN>
 constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem<BN>) + 1024; }  // + alignment slack
-
-// ---- PTX helpers ------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false (and the CTA marked failed) if the phase does not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* failed) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*failed) return false;
-    if (i > 32) __nanosleep(64);
-  }
-  *failed = 1;
-  return false;
-}
-// Bounded wait used on the way out: no early exit on the failure flag.
-__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return;
-    if (i > 32) __nanosleep(64);
-  }
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_addr(dst)),
-               "r"(cols));
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-}
-__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols));
-}
-__device__ __forceinline__ void fence_before_sync() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_after_sync() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// Shared-memory matrix descriptor: K-major tile with 128-byte rows, 128-byte swizzle; 8-row
-// groups 1024 bytes apart (SBO), leading offset 16 bytes, descriptor version 1.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_addr(bar))
-      : "memory");
-}
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 // ---- the shared mainloop + per-GEMM epilogue ------------------------------------------------
 enum GemmKind { kGemmSwiGLU = 0, kGemmDown = 1 };
@@ -283,7 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_base = a_base + kATileBytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            mma_bf16(acc, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
+            mma_kind_f16(acc, smem_desc(a_base + k * 32), smem_desc(b_base + k * 32),
                      GemmCfg<BN>::kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
           mma_commit(&sm.empty[s]);
         }
@@ -428,25 +318,6 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* out,
 }
 
 // ---- host side ---------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
 // The kernels need more than 48 KB of dynamic shared memory: opt in once per device.
 static cudaError_t allow_gemm_smem() {
   static std::mutex mu;
@@ -469,20 +340,6 @@ static cudaError_t allow_gemm_smem() {
     return e;
   done[dev] = true;
   return cudaSuccess;
-}
-
-// 2-D bf16 tensor [rows][cols] (row-major, cols contiguous) read in box_rows x 64 tiles.
-static bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                     uint32_t box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
-  const cuuint32_t elem[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Launch as a programmatic dependent of the previous kernel in the stream (the kernel calls

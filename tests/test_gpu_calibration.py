@@ -115,3 +115,32 @@ def test_reference_closed_form_clipping_and_errors():
         bad.update(torch.zeros(2, 2, dtype=torch.long, device=DEV), torch.zeros(2, 3, 8, device=DEV))
     with pytest.raises(RuntimeError):
         bad.update(torch.zeros(2, 2, dtype=torch.long), torch.zeros(2, 2, 8))
+
+
+@pytest.mark.parametrize("k", [1, 2, 4, 8])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_pass_matches_oracle(k, dtype):
+    """The tensor-core Gram pass (bf16 / fp16 outputs, k in {1, 2, 4, 8}, hidden a multiple of
+    128): token counts that leave a partial last block, out-of-range and repeated expert ids,
+    int32 and int64 ids, and an accumulation over two calls."""
+    rng = np.random.default_rng(100 + k)
+    E, H = 40, 256
+    for T, id_dtype in ((1, np.int64), (37, np.int32), (1000, np.int64)):
+        ids = rng.integers(0, E, (T, k)).astype(id_dtype)
+        if T > 3 and k > 1:
+            ids[1, 0] = -3
+            ids[2, k - 1] = E
+            ids[3, 1] = ids[3, 0]
+        out = rng.standard_normal((T, k, H)).astype(np.float32) * 0.7
+        out = torch.from_numpy(out).to(dtype).float().numpy()
+        stats = PairwiseScalarStats(E, device=DEV)
+        stats.update(cuda(ids), cuda(out, dtype))
+        stats.update(cuda(ids[::-1].copy()), cuda(out[::-1].copy(), dtype))
+        acc = C.new_accumulators(E)
+        C.update(acc, ids, out, E)
+        C.update(acc, ids[::-1], out[::-1], E)
+        close_stats(host(stats.dot), acc["dot"])
+        close_stats(host(stats.target_sq_norm), acc["target_sq"])
+        close_stats(host(stats.source_sq_norm), acc["source_sq"])
+        close_stats(host(stats.expert_norm_sum), acc["norm_sum"])
+        np.testing.assert_array_equal(host(stats.expert_norm_count), acc["norm_count"])
