@@ -6,23 +6,24 @@
 // fp32) by cp.async, three chunks in flight per warp; lane l copies and reads only its own
 // 16-byte unit of each row, so the pipeline needs no barrier.  Each lane accumulates the 36
 // pairwise dot products (squared norms on the diagonal) of its columns in fp32; a butterfly
-// reduction in a fixed order gives the token's totals.  The 56 ordered pairs of routes with different experts and the 8 norms are then split
-// over the lanes: each adds, in fp64, the fp32 products w_s <u_s, u_d>, w_s ||u_d||^2,
-// w_s ||u_s||^2 (w_s = ||u_s||) into the [E, E] statistics, and ||u_s|| and 1 into the
-// per-expert norm sum and count, with 64-bit atomics in L2 (the reference's index_add_).  The
-// pass is bound by reading the outputs; the fp32 dot products take about half that time.
+// reduction in a fixed order gives the token's totals.  The 56 ordered pairs of routes with
+// different experts and the 8 norms are then split over the lanes: each adds, in fp64, the fp32
+// products w_s <u_s, u_d>, w_s ||u_d||^2, w_s ||u_s||^2 (w_s = ||u_s||) into the [E, E]
+// statistics, and ||u_s|| and 1 into the per-expert norm sum and count, with 64-bit atomics in
+// L2 (the reference's index_add_).  The FMA chains make this pass issue-bound; it serves fp32
+// outputs and the shapes the tensor-core pass does not take.
 // calib_gram_kernel, the same update for bf16 / fp16 outputs with k in {1, 2, 4, 8} and a hidden
 // size that is a multiple of 128, on the tensor cores: 128 / k tokens' routes are 128 consecutive
 // rows of the [tokens * k, hidden] outputs, and one tcgen05.mma chain (M = N = 128, K = 16 per
 // instruction, fp32 in TMEM) computes their Gram matrix X X^T, with the same TMA-loaded tile as
 // both operands.  Only the 128 / k diagonal k x k blocks are used (1/16 of the products at k = 8),
-// which the tensor cores still do in less time than the tile takes to arrive from HBM, so the pass
-// runs at the HBM rate instead of being bound by 36 fp32 FMA chains per token.  The products are
-// exact in fp32; each 128-column slice is summed by the tensor core into one of 4 TMEM
-// accumulators in turn, and the slices' sums are added in fp32 with round-to-nearest (the tensor
-// core's own fp32 chains drop low bits, 1.8e-5 of a dot product over 2048 columns).  Warp roles as in moe_gemm.cu:
-// warp 0 streams 16 KB tiles through an 8-stage ring, warp 1 issues the MMAs, warps 2-5 read
-// their 32 rows' k columns from TMEM and add the same fp64 updates as calib_update_kernel.
+// which the tensor cores still do in less time than the tile takes to arrive from HBM.  The
+// products are exact in fp32; each 128-column slice is summed by the tensor core into one of 4
+// TMEM accumulators in turn, and the slices' sums are added in fp32 with round-to-nearest (the
+// tensor core's own fp32 chains drop low bits, 1.8e-5 of a dot product over 2048 columns).  Warp
+// roles as in moe_gemm.cu: warp 0 streams 16 KB tiles through an 8-stage ring, warp 1 issues
+// the MMAs, warps 2-5 read their 32 rows' k columns from TMEM and add the same fp64 updates as
+// calib_update_kernel.
 // calib_finalize_kernel (calibration.py:97-126): the closed form element by element in fp64,
 // a device flag for non-finite statistics.  calib_norms_kernel (calibration.py:128-140): mean
 // norm per expert, the lower median of the observed experts for the others.
