@@ -39,7 +39,7 @@ def routing(tokens, experts, top_k, gen):
     return (w / w.sum(-1, keepdim=True)).contiguous(), ids.to(torch.int32).contiguous()
 
 
-def run_case(tokens, experts, top_k, hidden, inter, seed):
+def run_case(tokens, experts, top_k, hidden, inter, seed, ids=None):
     gen = torch.Generator(device=DEV)
     gen.manual_seed(seed)
     x = torch.randn(tokens, hidden, generator=gen, device=DEV).to(torch.bfloat16)
@@ -47,6 +47,8 @@ def run_case(tokens, experts, top_k, hidden, inter, seed):
         torch.bfloat16)
     w2 = (0.02 * torch.randn(experts, hidden, inter, generator=gen, device=DEV)).to(torch.bfloat16)
     tw, ti = routing(tokens, experts, top_k, gen)
+    if ids is not None:
+        ti = ids.to(DEV, torch.int32).contiguous()
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     y = ops.fused_experts(x, tw, ti, w13, w2, status=status)
     ref = reference(x, tw, ti, w13, w2)
@@ -66,6 +68,22 @@ def test_small_shapes():
 def test_qwen3_decode_shape():
     """B=256 routed to E=128 experts, hidden 2048, intermediate 768 (the Qwen3 decode layer)."""
     run_case(tokens=256, experts=128, top_k=8, hidden=2048, inter=768, seed=4)
+
+
+def test_decode_tiles_block_fill_levels():
+    """Few routes per expert on average (the decode path: 128-wide N tile), with experts holding
+    1, 63, 64, 65, 128, 129 and 200 routes: nearly empty, half-full, full and split blocks."""
+    tokens, experts = 400, 64
+    counts = {0: 1, 1: 63, 2: 64, 3: 65, 4: 128, 5: 129, 6: 200}
+    slot0, slot1 = [], []
+    for e, c in counts.items():
+        (slot0 if len(slot0) + c <= tokens else slot1).extend([e] * c)
+    rng = torch.Generator().manual_seed(11)
+    fill0 = torch.randint(8, 36, (tokens - len(slot0),), generator=rng).tolist()
+    fill1 = torch.randint(36, 64, (tokens - len(slot1),), generator=rng).tolist()
+    ids = torch.stack([torch.tensor(slot0 + fill0), torch.tensor(slot1 + fill1)], 1)
+    perm = torch.randperm(tokens, generator=rng)
+    run_case(tokens, experts, 2, hidden=512, inter=256, seed=12, ids=ids[perm])
 
 
 def test_prefill_many_rows_per_expert():
