@@ -497,6 +497,25 @@ def run_extra(args) -> None:
                    weight_gbs=wbytes / ms / 1e6,
                    hbm_frac_of_measured_peak=wbytes / ms / 1e6 / peaks["hbm_gbs"],
                    status=int(status.item()), launches=7)
+        if args.workload == "moe_qwen3_decode" and not args.experts:
+            # the decode budget and the expert layer: two calls, and the fused entry (moe_align
+            # inside the decode launch, duplicate (token, expert) routes merged)
+            n, c, l_ = (torch.from_numpy(a).to(dev) for a in (lay.norms, lay.coeff, lay.loss))
+
+            def two_calls():
+                dw, di = ops.decode(rw, ri, n, c, l_, 64, variant="qwen3")
+                ops.fused_experts(x, dw, di, w13, w2, status=status)
+
+            def fused():
+                ops.decode_fused_experts(x, rw, ri, n, c, l_, 64, w13, w2, variant="qwen3",
+                                         status=status)
+
+            ms_two = _timed_graph(two_calls, steps, max(3, args.warmup), dev)
+            ms_fused = _timed_graph(fused, steps, max(3, args.warmup), dev)
+            merged = int((ids.sort(dim=1).values.diff(dim=1) == 0).sum().item())
+            out["decode_layer"] = {"us_decode_then_experts": ms_two * 1e3,
+                                   "us_decode_fused_experts": ms_fused * 1e3,
+                                   "merged_routes": merged, "status": int(status.item())}
     elif args.workload == "dsv4_prefill_fold":
         lay = W.layer("dsv4_prefill")
         coeff, loss = lay.coeff.copy(), lay.loss.copy()

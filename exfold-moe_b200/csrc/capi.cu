@@ -346,6 +346,46 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
   return cuda_status(launch_moe_experts(a, ws, (cudaStream_t)stream), name);
 }
 
+EXF_API int64_t exf_decode_fused_experts_workspace_bytes(int64_t batch, int top_k, int experts,
+                                                        int hidden, int inter) {
+  if (batch < 0 || top_k < 1 || experts < 1) return -1;
+  return decode_moe_workspace_bytes(batch, top_k, experts, hidden, inter);
+}
+
+EXF_API int exf_decode_fused_experts(const void* x, const float* w, const int32_t* ids,
+                                     int64_t batch, int top_k, int experts, int budget,
+                                     int variant, const float* norms, const float* coeff,
+                                     const float* loss, const void* w13, const void* w2,
+                                     int hidden, int inter, float* out_w, int32_t* out_ids,
+                                     void* y, void* workspace, int64_t workspace_bytes,
+                                     int32_t* status, exf_stream_t stream) {
+  const char* name = "exf_decode_fused_experts";
+  int rc = decode_checks(name, EXF_F32, EXF_I32, batch, top_k, experts, budget, variant);
+  if (rc != EXF_OK) return rc;
+  if (experts > kDecodeAlignMaxExperts || top_k > 8 ||
+      batch * top_k > (int64_t)kDecodeAlignMaxRoutes)
+    return fail(EXF_ERR_UNSUPPORTED,
+                "%s: at most %d experts, top_k <= 8 and %d routes (batch * top_k)", name,
+                kDecodeAlignMaxExperts, kDecodeAlignMaxRoutes);
+  if (hidden % 256 != 0 || inter % 128 != 0)
+    return fail(EXF_ERR_UNSUPPORTED,
+                "%s: hidden must be a multiple of 256 and intermediate a multiple of 128", name);
+  if (batch == 0) return EXF_OK;
+  EXF_REQUIRE(norms && coeff && loss, "%s: null calibration table", name);
+  EXF_REQUIRE(x && w && ids && w13 && w2 && out_w && out_ids && y && workspace,
+              "%s: null pointer", name);
+  EXF_REQUIRE(aligned16(x) && aligned16(w13) && aligned16(w2) && aligned16(y) &&
+                  aligned16(workspace),
+              "%s: tensors must be 16-byte aligned", name);
+  const int64_t need = decode_moe_workspace_bytes(batch, top_k, experts, hidden, inter);
+  EXF_REQUIRE(workspace_bytes >= need, "%s: workspace of %lld bytes required", name,
+              (long long)need);
+  DecodeParams d{w, ids, batch * top_k, experts, budget, variant, 0 /*from routes*/, norms,
+                 nullptr, nullptr, coeff, loss, out_w, out_ids, nullptr};
+  MoeArgs a{x, out_w, out_ids, batch, top_k, w13, w2, experts, hidden, inter, y, status};
+  return cuda_status(launch_decode_moe_experts(d, a, workspace, (cudaStream_t)stream), name);
+}
+
 // moe_align without any device allocation: the chunk-count table lives in the library's fixed
 // scratch array (exf::g_align_static_table) instead of a caller workspace.
 EXF_API int exf_moe_align_noalloc(const void* ids, int id_dtype, int64_t numel, int experts,

@@ -58,6 +58,14 @@ struct DecodeParams {
   void* out_w;
   void* out_ids;
   int32_t* out_subset;
+  // decode + moe_align in the same launch (launch_decode_align only): the routes that the table
+  // sent to one expert twice in a token become one route, and moe_align runs over the result
+  int top_k;
+  float* gemm_w;            // [routes] weights for the expert layer (merged in slot order)
+  int32_t* gemm_ids;        // [routes] expert of each route; -1 for a merged or invalid route
+  int32_t* sorted_ids;      // moe_align outputs over gemm_ids, 128-row blocks
+  int32_t* block_experts;
+  int32_t* num_post_pad;
 };
 
 struct AlignParams {
@@ -88,6 +96,11 @@ bool router_biased_eligible(int experts, int scoring, int fold, const RouterPara
 cudaError_t launch_router_biased(int fold, const RouterParams& p, cudaStream_t s);
 cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p, cudaStream_t s);
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s);
+// fp32 weights, int32 ids, experts <= kDecodeAlignMaxExperts, routes <= kDecodeAlignMaxRoutes,
+// top_k <= 8
+constexpr int kDecodeAlignMaxExperts = 256;
+constexpr int kDecodeAlignMaxRoutes = 8192;
+cudaError_t launch_decode_align(const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,
                               int64_t routes, int experts, const float* norms, int64_t* imp,
                               cudaStream_t s);

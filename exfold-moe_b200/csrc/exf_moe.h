@@ -60,5 +60,12 @@ int64_t moe_capacity(int64_t numel, int experts);
 MoeWorkspace moe_workspace(int64_t tokens, int top_k, int experts, int hidden, int inter,
                            void* base);
 cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s);
+// Decode expert budget (d: the exf_decode parameters; fp32 weights, int32 ids) followed by the
+// expert layer over its routes, with moe_align done inside the decode launch and duplicate
+// (token, expert) routes merged.  The workspace holds a MoeWorkspace then the merged routes.
+int64_t decode_moe_workspace_bytes(int64_t tokens, int top_k, int experts, int hidden,
+                                   int inter);
+cudaError_t launch_decode_moe_experts(DecodeParams d, const MoeArgs& a, void* workspace,
+                                      cudaStream_t s);
 
 }  // namespace exf

@@ -440,15 +440,11 @@ static cudaError_t launch_gemms(const MoeArgs& a, const MoeWorkspace& w, cudaStr
                     s, ma, mb, p);
 }
 
-cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+// Steps 2-5 of launch_moe_experts, from routes already aligned into w.
+static cudaError_t launch_moe_compute(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
   const int64_t numel = a.tokens * a.top_k;
   const int64_t cap = w.capacity;
   cudaError_t e = allow_gemm_smem();
-  if (e != cudaSuccess) return e;
-  // 1. moe_align with the GEMM's 128-row blocks
-  AlignParams ap{a.topk_ids, numel, a.experts, kBM, cap, w.sorted_ids, w.expert_ids,
-                 w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
-  e = launch_align(0 /*int32*/, ap, s);
   if (e != cudaSuccess) return e;
   // 2. gather token rows into route order
   {
@@ -476,6 +472,39 @@ cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStre
                       static_cast<const __nv_bfloat16*>(w.out), a.topk_ids, a.experts, a.tokens,
                       a.top_k, a.hidden, static_cast<__nv_bfloat16*>(a.y));
   }
+}
+
+cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+  // 1. moe_align with the GEMM's 128-row blocks
+  AlignParams ap{a.topk_ids, a.tokens * a.top_k, a.experts, kBM, w.capacity, w.sorted_ids,
+                 w.expert_ids, w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
+  const cudaError_t e = launch_align(0 /*int32*/, ap, s);
+  return e != cudaSuccess ? e : launch_moe_compute(a, w, s);
+}
+
+int64_t decode_moe_workspace_bytes(int64_t tokens, int top_k, int experts, int hidden,
+                                   int inter) {
+  return moe_workspace(tokens, top_k, experts, hidden, inter, nullptr).bytes +
+         2 * up256(tokens * top_k * 4);
+}
+
+cudaError_t launch_decode_moe_experts(DecodeParams d, const MoeArgs& a, void* workspace,
+                                      cudaStream_t s) {
+  const MoeWorkspace w = moe_workspace(a.tokens, a.top_k, a.experts, a.hidden, a.inter, workspace);
+  uint8_t* extra = static_cast<uint8_t*>(workspace) + w.bytes;
+  d.top_k = a.top_k;
+  d.gemm_w = reinterpret_cast<float*>(extra);
+  d.gemm_ids = reinterpret_cast<int32_t*>(extra + up256(a.tokens * a.top_k * 4));
+  d.sorted_ids = w.sorted_ids;
+  d.block_experts = w.expert_ids;
+  d.num_post_pad = w.num_post_pad;
+  // 1. decode and moe_align in one launch (the merged routes)
+  cudaError_t e = launch_decode_align(d, s);
+  if (e != cudaSuccess) return e;
+  MoeArgs m = a;
+  m.topk_w = d.gemm_w;
+  m.topk_ids = d.gemm_ids;
+  return launch_moe_compute(m, w, s);
 }
 
 }  // namespace exf

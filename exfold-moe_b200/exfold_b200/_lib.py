@@ -51,6 +51,9 @@ SIGNATURES = {
     "exf_fused_experts_workspace_bytes": (_i64, [_i64, _i, _i, _i, _i]),
     "exf_fused_experts": (_i, [_vp, _vp, _vp, _i64, _i, _vp, _vp, _i, _i, _i, _vp, _vp, _i64, _vp,
                                _vp]),
+    "exf_decode_fused_experts_workspace_bytes": (_i64, [_i64, _i, _i, _i, _i]),
+    "exf_decode_fused_experts": (_i, [_vp, _vp, _vp, _i64, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                                      _i, _i, _vp, _vp, _vp, _vp, _i64, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -272,6 +272,44 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
 
 
 # ---- grouped SwiGLU experts (tcgen05) ------------------------------------------------------------
+def decode_fused_experts(x: torch.Tensor, weights: torch.Tensor, ids: torch.Tensor,
+                         norms: torch.Tensor, coeff: torch.Tensor, loss: torch.Tensor, budget: int,
+                         w13: torch.Tensor, w2: torch.Tensor, *, variant: str = "qwen3",
+                         status: torch.Tensor | None = None
+                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Decode expert budget, then the expert layer over the remapped routes: returns
+    (y, w_out, ids_out).
+
+    `decode` followed by `fused_experts`, with moe_align done inside the decode launch and the
+    routes of a token that the budget sends to the same expert merged (weights summed, the
+    expert computed once).  w_out / ids_out equal `decode`'s outputs bit for bit (fp32 / int32);
+    y equals `fused_experts(x, w_out, ids_out, w13, w2)` within bf16 rounding.  At most 256
+    experts, top_k <= 8 and 8192 routes.
+    """
+    dev = _require_cuda(x, weights, ids, norms, coeff, loss, w13, w2)
+    if x.dtype != torch.bfloat16 or w13.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16:
+        raise TypeError("decode_fused_experts computes in bf16: x, w13 and w2 must be bfloat16")
+    x, w13, w2 = x.contiguous(), w13.contiguous(), w2.contiguous()
+    w_in = weights.float().contiguous()
+    i_in = ids.to(torch.int32).contiguous()
+    batch, top_k = w_in.shape
+    hidden = x.shape[1]
+    experts, two_i, _ = w13.shape
+    inter = two_i // 2
+    norms, coeff, loss = _f32c(norms), _f32c(coeff), _f32c(loss)
+    ow, oi = torch.empty_like(w_in), torch.empty_like(i_in)
+    y = torch.empty_like(x)
+    ws_bytes = int(L.lib().exf_decode_fused_experts_workspace_bytes(batch, top_k, experts,
+                                                                    hidden, inter))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    L.check(L.lib().exf_decode_fused_experts(
+        x.data_ptr(), w_in.data_ptr(), i_in.data_ptr(), batch, top_k, experts, int(budget),
+        _VARIANT[variant], norms.data_ptr(), coeff.data_ptr(), loss.data_ptr(), w13.data_ptr(),
+        w2.data_ptr(), hidden, inter, ow.data_ptr(), oi.data_ptr(), y.data_ptr(), ws.data_ptr(),
+        ws_bytes, _ptr(status), _stream(dev)))
+    return y, ow, oi
+
+
 def fused_experts(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
                   w13: torch.Tensor, w2: torch.Tensor,
                   status: torch.Tensor | None = None) -> torch.Tensor:

@@ -183,6 +183,28 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
                               int experts, int hidden, int inter, void* y, void* workspace,
                               int64_t workspace_bytes, int32_t* status, exf_stream_t stream);
 
+/* Decode expert budget followed by the expert layer, with the routing between them fused
+ * (the scope table's first "next" row): select_and_reroute_decode / exfold_decode_cuda
+ * (exfold/qwen3/kernels.py:423-491; exfold_kernels.cu:280-322), then vLLM moe_align_block_size
+ * (moe_align_block_size.py:11-93) and fused_experts (fused_moe.py:1587) over the remapped routes.
+ * The decode launch also merges the routes of a token that the table sent to the same expert
+ * (their weights summed in slot order, the expert computed once) and writes the moe_align
+ * outputs for the merged routes, so the layer is that launch plus gather, two GEMMs and combine.
+ * out_w / out_ids [batch][top_k] receive exf_decode's outputs bit for bit; y bf16
+ * [batch][hidden] equals exf_fused_experts over them within bf16 rounding (a merged route's
+ * output is rounded once instead of twice).  w fp32, ids int32; experts <= 256, top_k <= 8,
+ * batch * top_k <= 8192; other arguments as exf_decode and exf_fused_experts.  workspace:
+ * exf_decode_fused_experts_workspace_bytes(), 16-byte aligned. */
+EXF_API int64_t exf_decode_fused_experts_workspace_bytes(int64_t batch, int top_k, int experts,
+                                                        int hidden, int inter);
+EXF_API int exf_decode_fused_experts(const void* x, const float* w, const int32_t* ids,
+                                     int64_t batch, int top_k, int experts, int budget,
+                                     int variant, const float* norms, const float* coeff,
+                                     const float* loss, const void* w13, const void* w2,
+                                     int hidden, int inter, float* out_w, int32_t* out_ids,
+                                     void* y, void* workspace, int64_t workspace_bytes,
+                                     int32_t* status, exf_stream_t stream);
+
 /* Calibration statistics (offline): the GPU form of PairwiseScalarStats
  * (exfold/qwen3/calibration.py:9-140), which builds the [E][E] coefficient / loss tables and the
  * expert norms that the folds above read.

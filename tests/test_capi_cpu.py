@@ -81,6 +81,14 @@ def test_argument_validation_without_gpu():
     assert rc == L.EXF_ERR_INVALID and "workspace" in last_error()
     rc = call("exf_moe_align", fake, 0, 100, 2048, 64, 10 ** 6, fake, fake, fake, None, 0, None)
     assert rc == L.EXF_ERR_UNSUPPORTED
+    # decode fused with the expert layer: experts, routes and the workspace are bounded
+    dfe = lambda batch, k, e, ws: call(  # noqa: E731
+        "exf_decode_fused_experts", fake, fake, fake, batch, k, e, 8, 0, fake, fake, fake, fake,
+        fake, 256, 128, fake, fake, fake, fake, ws, None, None)
+    assert dfe(4, 8, 512, 1 << 30) == L.EXF_ERR_UNSUPPORTED and "256" in last_error()
+    assert dfe(2048, 8, 128, 1 << 30) == L.EXF_ERR_UNSUPPORTED and "8192" in last_error()
+    assert dfe(4, 8, 128, 16) == L.EXF_ERR_INVALID and "workspace" in last_error()
+    assert dfe(0, 8, 128, 0) == 0
 
 
 def test_empty_inputs_are_no_ops_without_gpu():
