@@ -351,14 +351,35 @@ def run_ours(args) -> None:
     host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
     host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
     dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.float32, device=dev)
+    dev_w = torch.empty((2, TOKENS, KEEP), dtype=torch.float32, device=dev)
+    dev_i = torch.empty((2, TOKENS, KEEP), dtype=torch.int32, device=dev)
+    # Host->device copies, the router calls and device->host copies on three streams, double
+    # buffered, so that layer l's results go back while layer l+1's logits come in (PCIe runs
+    # both directions at once).  Every copy of the step stays inside the timed region.
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # logits of buffer b are on the device
+    ev_done = [torch.cuda.Event() for _ in range(2)]  # the call reading buffer b has finished
+    ev_back = [torch.cuda.Event() for _ in range(2)]  # results of buffer b are on the host
 
     def e2e_step():
+        copy_in.wait_stream(stream)
         for layer in range(LAYERS):
-            buf = dev_in[layer % 2]
-            buf.copy_(host_in[layer % slots], non_blocking=True)
-            w, i = ops.router_fold_prefill(buf, TOP_K, KEEP, coeff[layer], loss[layer])
-            host_w[layer % slots].copy_(w, non_blocking=True)
-            host_i[layer % slots].copy_(i, non_blocking=True)
+            b = layer % 2
+            copy_in.wait_event(ev_done[b])
+            with torch.cuda.stream(copy_in):
+                dev_in[b].copy_(host_in[layer % slots], non_blocking=True)
+            ev_in[b].record(copy_in)
+            stream.wait_event(ev_in[b])
+            stream.wait_event(ev_back[b])
+            ops.router_fold_prefill(dev_in[b], TOP_K, KEEP, coeff[layer], loss[layer],
+                                    out=(dev_w[b], dev_i[b]))
+            ev_done[b].record(stream)
+            copy_out.wait_event(ev_done[b])
+            with torch.cuda.stream(copy_out):
+                host_w[layer % slots].copy_(dev_w[b], non_blocking=True)
+                host_i[layer % slots].copy_(dev_i[b], non_blocking=True)
+            ev_back[b].record(copy_out)
+        stream.wait_stream(copy_out)
 
     e2e_steps = max(2, min(10, args.steps // 100))
     saved_warmup = args.warmup
