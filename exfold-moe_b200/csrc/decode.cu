@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(256) static_remap_kernel(void* wv, void* idv, 
 }
 
 // ---------------------------------------------------------------------------------------------
-template <typename WT, typename IT>
+template <typename WT, typename IT, bool ALIGN = false>
 static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
@@ -517,22 +517,12 @@ static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<WT, IT>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<WT, IT, ALIGN>, p);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_decode_align(const DecodeParams& p, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
-  cfg.blockDim = dim3(kDecodeThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<float, int32_t, true>, p);
-  return e != cudaSuccess ? e : cudaGetLastError();
+  return launch_decode_t<float, int32_t, true>(p, s);
 }
 
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s) {
