@@ -80,3 +80,77 @@ def test_decode_policies(monkeypatch, policy):
     wa, ia = call(rall, x)
     np.testing.assert_array_equal(ia, ei)
     np.testing.assert_array_equal(wa, ew)
+
+
+# ---- DeepSeek-V4 (exfold/deepseek_v4/vllm_patch.py:213-368) ----------------------------------
+def dsv4_setup(seed, tokens, hash_table=False):
+    import types
+
+    lay = W.Layer(seed=seed, tokens=tokens, experts=256, top_k=8, kind="dsv4")
+    coeff, loss = lay.coeff.copy(), lay.loss.copy()
+    np.fill_diagonal(coeff, 1.0)
+    np.fill_diagonal(loss, 1e30)
+    conf = loss.copy()
+    np.fill_diagonal(conf, 0.0)
+    calib = tuple(torch.from_numpy(a[None].copy())
+                  for a in (coeff, loss, conf, coeff, loss, lay.norms))
+    rng = np.random.default_rng(seed)
+    table = np.stack([rng.permutation(256)[:8] for _ in range(1000)]).astype(np.int32)
+    gate = types.SimpleNamespace(e_score_correction_bias=torch.from_numpy(lay.bias).to(DEV),
+                                 tid2eid=torch.from_numpy(table).to(DEV) if hash_table else None)
+    module = types.SimpleNamespace(n_activated_experts=8, n_routed_experts=256,
+                                   scoring_func="sigmoid", renormalize=True,
+                                   routed_scaling_factor=2.5, gate=gate)
+    token_ids = rng.integers(0, 1000, tokens)
+    return lay, module, calib, (coeff, loss, conf), table, token_ids
+
+
+def test_dsv4_prefill_decode_and_mixed(monkeypatch):
+    from exfold_b200.deepseek_v4.router import make_router as make_dsv4
+
+    monkeypatch.setenv("EXFOLD_PREFILL_TOPK", "3")
+    monkeypatch.setenv("EXFOLD_PREFILL_RENORM", "similarity_blend")
+    monkeypatch.setenv("EXFOLD_DECODE_EXPERT_BUDGET", "64")
+    lay, module, calib, (coeff, loss, conf), _, _ = dsv4_setup(51, 128)
+    x = lay.logits
+    rw, ri = O.router_topk(x, 8, "sigmoid", lay.bias, True, 2.5)
+    pw, pi = O.fold_dsv4(rw, ri, coeff, loss, conf, 3, 2)
+    for counts, (ew, ei) in (((0, 128), (pw, pi)),
+                             ((128, 0), O.decode_dsv4(rw, ri, lay.norms, coeff, loss, 64))):
+        r = make_dsv4(module, 0, calib, counts_fn=lambda t, c=counts: c)
+        w, ids = call(r, x)
+        np.testing.assert_array_equal(ids, ei)
+        np.testing.assert_array_equal(w, ew)
+    # mixed: 40 decode tokens first, 88 prefill tokens after, prefill padded to 8 slots
+    r = make_dsv4(module, 0, calib, counts_fn=lambda t: (40, t - 40))
+    w, ids = call(r, x)
+    dw, di = O.decode_dsv4(rw[:40], ri[:40], lay.norms, coeff, loss, 64)
+    np.testing.assert_array_equal(ids[:40], di)
+    np.testing.assert_array_equal(w[:40], dw)
+    np.testing.assert_array_equal(ids[40:, :3], pi[40:])
+    np.testing.assert_array_equal(w[40:, :3], pw[40:])
+    np.testing.assert_array_equal(ids[40:, 3:], np.repeat(pi[40:, 2:3], 5, axis=1))
+    assert not w[40:, 3:].any()
+    # a decode batch whose routes fit in the budget keeps them
+    r = make_dsv4(module, 0, calib, counts_fn=lambda t: (t, 0))
+    w, ids = call(r, x[:8])
+    np.testing.assert_array_equal(ids, ri[:8])
+    np.testing.assert_array_equal(w, rw[:8])
+
+
+def test_dsv4_hash_layer_prefill(monkeypatch):
+    from exfold_b200.deepseek_v4.router import make_router as make_dsv4
+
+    monkeypatch.setenv("EXFOLD_PREFILL_TOPK", "3")
+    monkeypatch.setenv("EXFOLD_PREFILL_RENORM", "router_l2")
+    lay, module, calib, (coeff, loss, conf), table, token_ids = dsv4_setup(52, 300, True)
+    r = make_dsv4(module, 0, calib, counts_fn=lambda t: (0, t))
+    w, ids = r(None, torch.from_numpy(lay.logits).to(DEV), 8, True,
+               input_ids=torch.from_numpy(token_ids).to(DEV))
+    torch.cuda.synchronize()
+    hw, hi = O.router_hash(lay.logits, token_ids, table, "sigmoid", True, 2.5)
+    ew, ei = O.fold_dsv4(hw, hi, coeff, loss, conf, 3, 1)
+    np.testing.assert_array_equal(ids.cpu().numpy(), ei)
+    np.testing.assert_array_equal(w.cpu().numpy(), ew)
+    with pytest.raises(RuntimeError, match="input_ids"):
+        r(None, torch.from_numpy(lay.logits).to(DEV), 8, True)

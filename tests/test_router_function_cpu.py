@@ -46,3 +46,33 @@ def test_decode_policy_is_checked(monkeypatch):
         R.make_router(t, t, torch.ones(4), 4, 2)
     monkeypatch.setenv("EXFOLD_QWEN3_DECODE_POLICY", "STATIC_NORM")
     assert callable(R.make_router(t, t, torch.ones(4), 4, 2))
+
+
+# ---- DeepSeek-V4 (exfold/deepseek_v4/vllm_patch.py:30-70, 213-368) ---------------------------
+def test_dsv4_phase_counts_and_padding():
+    from exfold_b200.deepseek_v4 import router as D
+
+    nested = {"x": [None, {"y": meta(6, 2)}]}
+    assert D.find_phase_metadata(nested).num_prefill_tokens == 6
+    assert D.phase_token_counts(8, metadata=nested) == (2, 6)
+    with pytest.raises(RuntimeError, match="mismatch"):
+        D.phase_token_counts(9, metadata=nested)
+    assert D.phase_token_counts(5, unavailable=(0, 5), metadata={"x": 1}) == (0, 5)
+    with pytest.raises(RuntimeError, match="unavailable"):
+        D.phase_token_counts(5, metadata=[])
+    w = torch.tensor([[0.5, 0.25, 0.125]])
+    ids = torch.tensor([[7, 3, 9]], dtype=torch.int32)
+    pw, pi = D.pad_routes(w, ids, 5)
+    assert pw.tolist() == [[0.5, 0.25, 0.125, 0.0, 0.0]] and pi.tolist() == [[7, 3, 9, 9, 9]]
+    assert D.pad_routes(w, ids, 3)[1] is ids
+
+
+def test_dsv4_renorm_mode_is_checked(monkeypatch):
+    from exfold_b200.deepseek_v4 import router as D
+
+    module = types.SimpleNamespace(n_activated_experts=8, n_routed_experts=256)
+    monkeypatch.setenv("EXFOLD_PREFILL_RENORM", "softmax")
+    with pytest.raises(ValueError, match="EXFOLD_PREFILL_RENORM"):
+        D.make_router(module, 0, None)
+    monkeypatch.setenv("EXFOLD_PREFILL_RENORM", "Similarity_Blend")
+    assert D.make_router(module, 0, None)._dsv4_accepts_input_ids
