@@ -292,22 +292,38 @@ EXF_API int64_t exf_moe_align_workspace_bytes(int64_t numel, int experts) {
   return align_workspace_bytes(numel, experts);
 }
 
-EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int experts,
-                          int block_size, int64_t capacity, int32_t* sorted_ids,
-                          int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
-                          int64_t workspace_bytes, exf_stream_t stream) {
-  const char* name = "exf_moe_align";
+// Checks shared by the two moe_align entry points.  The kernels keep expert offsets, the padded
+// total and block starts in int32, so the padded total (at most the capacity formula) and the
+// capacity must stay below 2^31.
+static int align_checks(const char* name, const void* ids, int id_dtype, int64_t numel,
+                        int experts, int block_size, int64_t capacity, const int32_t* sorted_ids,
+                        const int32_t* expert_ids, const int32_t* num_post_pad) {
   EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported id dtype", name);
   EXF_REQUIRE(numel >= 0 && numel < (int64_t)1 << 31, "%s: numel out of range", name);
   EXF_REQUIRE(block_size >= 1, "%s: block_size must be >= 1", name);
   if (experts < 1 || experts > align_max_experts())
     return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
-  EXF_REQUIRE(capacity >= exf_moe_align_capacity(numel, experts, block_size, 0) ||
-                  capacity >= numel * (int64_t)block_size,
+  const int64_t padded = exf_moe_align_capacity(numel, experts, block_size, 0);
+  EXF_REQUIRE(padded < ((int64_t)1 << 31) && capacity < ((int64_t)1 << 31),
+              "%s: %lld routes over %d experts in blocks of %d (capacity %lld) exceed the int32 "
+              "offsets: the padded total and the capacity must be below 2^31",
+              name, (long long)numel, experts, block_size, (long long)capacity);
+  EXF_REQUIRE(capacity >= padded || capacity >= numel * (int64_t)block_size,
               "%s: capacity too small", name);
   EXF_REQUIRE(num_post_pad && (capacity == 0 || (sorted_ids && expert_ids)), "%s: null output",
               name);
   EXF_REQUIRE(numel == 0 || ids, "%s: null ids", name);
+  return EXF_OK;
+}
+
+EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int experts,
+                          int block_size, int64_t capacity, int32_t* sorted_ids,
+                          int32_t* expert_ids, int32_t* num_post_pad, void* workspace,
+                          int64_t workspace_bytes, exf_stream_t stream) {
+  const char* name = "exf_moe_align";
+  const int rc = align_checks(name, ids, id_dtype, numel, experts, block_size, capacity,
+                              sorted_ids, expert_ids, num_post_pad);
+  if (rc != EXF_OK) return rc;
   const int64_t need = align_workspace_bytes(numel, experts);
   EXF_REQUIRE(need == 0 || (workspace && workspace_bytes >= need),
               "%s: workspace of %lld bytes required", name, (long long)need);
@@ -327,8 +343,9 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
                               int experts, int hidden, int inter, void* y, void* workspace,
                               int64_t workspace_bytes, int32_t* status, exf_stream_t stream) {
   const char* name = "exf_fused_experts";
-  EXF_REQUIRE(tokens >= 0 && top_k >= 1 && tokens * top_k < ((int64_t)1 << 31),
-              "%s: bad routing shape", name);
+  EXF_REQUIRE(tokens >= 0 && top_k >= 1 &&
+                  tokens * top_k + (int64_t)experts * 127 < ((int64_t)1 << 31),
+              "%s: bad routing shape (routes plus block padding must stay below 2^31)", name);
   if (experts < 1 || experts > align_max_experts())
     return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
   if (hidden % 256 != 0 || inter % 128 != 0)
@@ -393,17 +410,9 @@ EXF_API int exf_moe_align_noalloc(const void* ids, int id_dtype, int64_t numel, 
                                   int32_t* expert_ids, int32_t* num_post_pad,
                                   exf_stream_t stream) {
   const char* name = "exf_moe_align_noalloc";
-  EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported id dtype", name);
-  EXF_REQUIRE(numel >= 0 && numel < (int64_t)1 << 31, "%s: numel out of range", name);
-  EXF_REQUIRE(block_size >= 1, "%s: block_size must be >= 1", name);
-  if (experts < 1 || experts > align_max_experts())
-    return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
-  EXF_REQUIRE(capacity >= exf_moe_align_capacity(numel, experts, block_size, 0) ||
-                  capacity >= numel * (int64_t)block_size,
-              "%s: capacity too small", name);
-  EXF_REQUIRE(num_post_pad && (capacity == 0 || (sorted_ids && expert_ids)), "%s: null output",
-              name);
-  EXF_REQUIRE(numel == 0 || ids, "%s: null ids", name);
+  const int rc = align_checks(name, ids, id_dtype, numel, experts, block_size, capacity,
+                              sorted_ids, expert_ids, num_post_pad);
+  if (rc != EXF_OK) return rc;
   const int64_t entries = align_workspace_bytes(numel, experts) / (int64_t)sizeof(int32_t);
   const int64_t limit = align_static_table_ints();
   if (entries > limit) {

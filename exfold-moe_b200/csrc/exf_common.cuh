@@ -138,11 +138,13 @@ __device__ __forceinline__ bool ranks_before(uint32_t ka, int ia, uint32_t kb, i
   return ka > kb || (ka == kb && ia < ib);
 }
 
-// Decode importance in 2^-32 fixed point: fp32 product, clamp to |p| <= 2^30, round to nearest
-// even.  Integer sums are exact, so the result does not depend on summation order or on how a
-// batch is split over GPUs.
+// Decode importance in 2^-32 fixed point: fp32 product, a NaN product counts 0, clamp to
+// |p| <= 2^24 (so one route adds at most 2^56), round to nearest even.  Integer sums are exact
+// and wrap modulo 2^64, so an expert's importance is exact, whatever the summation order or the
+// split of the batch over GPUs, while its true total stays below 2^31 in magnitude.
 __device__ __forceinline__ long long fixed_point(float p) {
-  p = fminf(fmaxf(p, -1073741824.0f), 1073741824.0f);
+  if (p != p) return 0;
+  p = fminf(fmaxf(p, -16777216.0f), 16777216.0f);
   return __float2ll_rn(__fmul_rn(p, 4294967296.0f));
 }
 

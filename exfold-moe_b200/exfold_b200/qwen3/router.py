@@ -64,6 +64,9 @@ def make_router(coefficient: torch.Tensor, loss: torch.Tensor, norms: torch.Tens
     if policy not in {"dynamic", "static_norm"}:
         raise ValueError("EXFOLD_QWEN3_DECODE_POLICY must be 'dynamic' or 'static_norm'")
     experts = int(coefficient.shape[0])
+    if policy == "static_norm" and decode_budget < experts and decode_budget < 1:
+        # the reference builds the static table here and fails on an empty retained set
+        raise ValueError("decode_budget must be >= 1 for the static_norm decode policy")
     tables: dict[torch.device, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
     static: dict[torch.device, tuple[torch.Tensor, torch.Tensor]] = {}
 
@@ -102,7 +105,9 @@ def make_router(coefficient: torch.Tensor, loss: torch.Tensor, norms: torch.Tens
                     target, scale = static_for(gating_output.device, decode_budget)
                     w, ids = ops.static_remap_(w, ids, target, scale)
                 else:
-                    w, ids = ops.decode(w, ids, n, c, l_, subset, variant="qwen3")
+                    # select_and_reroute_decode clamps the subset to [1, E]
+                    # (exfold/qwen3/kernels.py:447)
+                    w, ids = ops.decode(w, ids, n, c, l_, max(1, subset), variant="qwen3")
         return w.float(), ids.int()
 
     router.experts = experts

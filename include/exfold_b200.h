@@ -158,7 +158,8 @@ EXF_API int exf_static_remap(void* w, int w_dtype, void* ids, int id_dtype, int6
  * capacity = exf_moe_align_capacity(); sorted_ids [capacity], expert_ids [ceil(capacity /
  * block_size)], num_post_pad [1].  Routes of one expert keep ascending flat order; padding
  * holds `numel`; unused blocks hold expert -1.  `workspace` (exf_moe_align_workspace_bytes
- * bytes, any contents) may be NULL when that size is 0. */
+ * bytes, any contents) may be NULL when that size is 0.  Offsets are int32: the padded total
+ * numel + experts * (block_size - 1) and the capacity must be below 2^31 (EXF_ERR_INVALID). */
 EXF_API int64_t exf_moe_align_capacity(int64_t numel, int experts, int block_size,
                                        int pad_sorted);
 EXF_API int64_t exf_moe_align_workspace_bytes(int64_t numel, int experts);
@@ -183,8 +184,8 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
                               int experts, int hidden, int inter, void* y, void* workspace,
                               int64_t workspace_bytes, int32_t* status, exf_stream_t stream);
 
-/* Decode expert budget followed by the expert layer, with the routing between them fused
- * (the scope table's first "next" row): select_and_reroute_decode / exfold_decode_cuda
+/* Decode expert budget followed by the expert layer, with the routing between them fused into
+ * the decode launch: select_and_reroute_decode / exfold_decode_cuda
  * (exfold/qwen3/kernels.py:423-491; exfold_kernels.cu:280-322), then vLLM moe_align_block_size
  * (moe_align_block_size.py:11-93) and fused_experts (fused_moe.py:1587) over the remapped routes.
  * The decode launch also merges the routes of a token that the table sent to the same expert
@@ -250,7 +251,9 @@ EXF_API int exf_calibration_norms(const double* norm_sum, const double* norm_cou
  * EXF_ERR_INVALID and a message, never truncated.
  * Set-up: the first call on each device looks up the array's device address (one
  * cudaGetSymbolAddress with that device current); make that first call before any stream
- * capture.
+ * capture.  The address is kept for the life of the process: after cudaDeviceReset (or
+ * anything else that destroys the device's primary context) do not call this entry point on
+ * that device again.
  * Sharing: all calls on a device use the same array and it keeps the last call's contents (each
  * call rewrites every entry it reads, so nothing needs clearing).  Calls whose kernels overlap on
  * the GPU (different streams, or concurrent graphs) race on the array; serialise them.

@@ -313,11 +313,15 @@ ORC_API void orc_fold_dsv4(const float* w, const int32_t* ids, int64_t tokens, i
 /* Decode importance.  The reference sums w * norm[e] with float atomics
  * (exfold/qwen3/kernels.py:369-398; exfold_kernels.cu:146-151), whose order
  * is not fixed.  Here each product is formed in fp32 (one rounding), clamped
- * to |p| <= 2^30, converted to a 2^-32 fixed point with round-to-nearest-even
+ * as below, converted to a 2^-32 fixed point with round-to-nearest-even
  * and summed in int64: exact and independent of order and of how the batch is
- * split across GPUs. */
+ * split across GPUs.  A NaN product counts 0 (the reference's fp32 sum would
+ * turn NaN and rank that expert first); products are clamped to |p| <= 2^24,
+ * so one route adds at most 2^56 and the int64 sum, which wraps modulo 2^64,
+ * is exact while an expert's true total stays below 2^31 in magnitude. */
 ORC_API int64_t orc_fixed_point(float p) {
-  p = fminf(fmaxf(p, -1073741824.0f), 1073741824.0f);
+  if (p != p) return 0;
+  p = fminf(fmaxf(p, -16777216.0f), 16777216.0f);
   return (int64_t)llrintf(p * 4294967296.0f);
 }
 
@@ -327,7 +331,9 @@ ORC_API void orc_importance(const float* w, const int32_t* ids, int64_t routes,
   for (int64_t r = 0; r < routes; ++r) {
     const int e = ids[r];
     if (e < 0 || e >= experts) continue;
-    importance[e] += orc_fixed_point(w[r] * norms[e]);
+    /* modulo 2^64, as the kernels' int64 atomics (signed overflow is undefined in C) */
+    importance[e] = (int64_t)((uint64_t)importance[e] +
+                              (uint64_t)orc_fixed_point(w[r] * norms[e]));
   }
 }
 

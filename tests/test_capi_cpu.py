@@ -81,6 +81,15 @@ def test_argument_validation_without_gpu():
     assert rc == L.EXF_ERR_INVALID and "workspace" in last_error()
     rc = call("exf_moe_align", fake, 0, 100, 2048, 64, 10 ** 6, fake, fake, fake, None, 0, None)
     assert rc == L.EXF_ERR_UNSUPPORTED
+    # offsets are int32: a padded total or a capacity of 2^31 or more is refused by both entry
+    # points (numel + experts * (block_size - 1) >= 2^31 here)
+    for name, extra in (("exf_moe_align", (None, 0)), ("exf_moe_align_noalloc", ())):
+        cap = L.lib().exf_moe_align_capacity(1000, 512, 1 << 22, 0)
+        assert cap >= 1 << 31
+        rc = call(name, fake, 0, 1000, 512, 1 << 22, cap, fake, fake, fake, *extra, None)
+        assert rc == L.EXF_ERR_INVALID and "2^31" in last_error(), name
+        rc = call(name, fake, 0, 1000, 128, 64, 1 << 31, fake, fake, fake, *extra, None)
+        assert rc == L.EXF_ERR_INVALID and "2^31" in last_error(), name
     # decode fused with the expert layer: experts, routes and the workspace are bounded
     dfe = lambda batch, k, e, ws: call(  # noqa: E731
         "exf_decode_fused_experts", fake, fake, fake, batch, k, e, 8, 0, fake, fake, fake, fake,

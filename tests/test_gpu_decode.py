@@ -203,3 +203,32 @@ def test_decode_edge_cases():
     ew, ei = O.decode_dsv4(np.ones_like(rw), ri2, np.ones(128, np.float32), lay.coeff, lay.loss, 1)
     np.testing.assert_array_equal(got, ei)
     np.testing.assert_array_equal(host(ow), ew)
+
+
+@pytest.mark.parametrize("variant", ["qwen3", "dsv4"])
+def test_decode_nan_and_huge_products(variant):
+    """A NaN product counts 0 and products are clamped to 2^24 in the importance, as in the
+    oracle; the fused decode, the importance pass and the split decode agree with it."""
+    lay = W.layer("qwen3_decode", tokens=64)
+    rw, ri = O.router_topk(lay.logits, 8, "softmax")
+    w = rw.copy()
+    w[0, 0] = np.nan
+    w[1, 1] = 1e30
+    w[2, :] = np.inf
+    w[3, 2] = 3.0e7  # above the clamp
+    coeff, loss = (lay.coeff, lay.loss) if variant == "qwen3" else dsv4_tables(lay)
+    ow, oi = ops.decode(cuda(w), cuda(ri), cuda(lay.norms), cuda(coeff), cuda(loss), 16,
+                        variant=variant)
+    if variant == "qwen3":
+        ew, ei, _ = O.decode_qwen3(w, ri, lay.norms, coeff, loss, 16)
+    else:
+        ew, ei = O.decode_dsv4(w, ri, lay.norms, coeff, loss, 16)
+    np.testing.assert_array_equal(host(oi), ei)
+    np.testing.assert_array_equal(host(ow), ew)
+    imp = torch.zeros(128, dtype=torch.int64, device=DEV)
+    ops.decode_importance(cuda(w), cuda(ri), cuda(lay.norms), imp)
+    np.testing.assert_array_equal(host(imp), O.importance(w, ri, lay.norms))
+    sw, si = ops.decode_apply(imp, cuda(w), cuda(ri), cuda(coeff), cuda(loss), 16,
+                              variant=variant)
+    np.testing.assert_array_equal(host(si), ei)
+    np.testing.assert_array_equal(host(sw), ew)

@@ -48,6 +48,28 @@ def test_decode_policy_is_checked(monkeypatch):
     assert callable(R.make_router(t, t, torch.ones(4), 4, 2))
 
 
+def test_decode_budget_below_one(monkeypatch):
+    """select_and_reroute_decode clamps the subset to [1, E] (exfold/qwen3/kernels.py:447): a
+    dynamic-policy budget of 0 or less decodes with a subset of 1; the static policy refuses it
+    when the router is made (the reference's table build fails there)."""
+    t = torch.zeros(8, 8)
+    monkeypatch.setenv("EXFOLD_QWEN3_DECODE_POLICY", "static_norm")
+    for budget in (0, -3):
+        with pytest.raises(ValueError, match="decode_budget"):
+            R.make_router(t, t, torch.ones(8), 4, budget)
+    monkeypatch.setenv("EXFOLD_QWEN3_DECODE_POLICY", "dynamic")
+    seen = []
+    monkeypatch.setattr(R.ops, "router_topk", lambda logits, k, **kw: (
+        torch.full((logits.shape[0], k), 1.0 / k), torch.zeros(logits.shape[0], k,
+                                                                dtype=torch.int32)))
+    monkeypatch.setattr(R.ops, "decode", lambda w, ids, n, c, l_, budget, **kw: (
+        seen.append(budget), (w, ids))[1])
+    for budget in (0, -3, 2):
+        router = R.make_router(t, t, torch.ones(8), 4, budget, phase_fn=lambda n: "decode")
+        router(None, torch.zeros(3, 8), 2, True)
+    assert seen == [1, 1, 2]
+
+
 # ---- DeepSeek-V4 (exfold/deepseek_v4/vllm_patch.py:30-70, 213-368) ---------------------------
 def test_dsv4_phase_counts_and_padding():
     from exfold_b200.deepseek_v4 import router as D

@@ -38,13 +38,16 @@ def stream():
     return ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
 
 
+def id_dtype(ids: torch.Tensor) -> int:
+    return L.EXF_I64 if ids.dtype == torch.int64 else L.EXF_I32
+
+
 def with_workspace(ids: torch.Tensor, experts: int, block: int):
     numel = ids.numel()
     cap, s, e, n = outputs(numel, experts, block)
     ws_bytes = int(L.lib().exf_moe_align_workspace_bytes(numel, experts))
-    assert ws_bytes > 0, "case too small to exercise the scratch"
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
-    L.check(L.lib().exf_moe_align(ids.data_ptr(), L.EXF_I32, numel, experts, block, cap,
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=DEV)
+    L.check(L.lib().exf_moe_align(ids.data_ptr(), id_dtype(ids), numel, experts, block, cap,
                                   s.data_ptr(), e.data_ptr(), n.data_ptr(), ws.data_ptr(),
                                   ws_bytes, stream()))
     return s, e, n
@@ -53,9 +56,19 @@ def with_workspace(ids: torch.Tensor, experts: int, block: int):
 def without_allocation(ids: torch.Tensor, experts: int, block: int):
     numel = ids.numel()
     cap, s, e, n = outputs(numel, experts, block)
-    L.check(L.lib().exf_moe_align_noalloc(ids.data_ptr(), L.EXF_I32, numel, experts, block, cap,
-                                          s.data_ptr(), e.data_ptr(), n.data_ptr(), stream()))
+    L.check(L.lib().exf_moe_align_noalloc(ids.data_ptr(), id_dtype(ids), numel, experts, block,
+                                          cap, s.data_ptr(), e.data_ptr(), n.data_ptr(),
+                                          stream()))
     return s, e, n
+
+
+def check_equal(ids: torch.Tensor, experts: int, block: int):
+    ref = with_workspace(ids, experts, block)
+    got = without_allocation(ids, experts, block)
+    torch.cuda.synchronize(DEV)
+    for r, g in zip(ref, got):
+        assert torch.equal(r, g)
+    assert int(got[2].item()) >= ids.numel()
 
 
 def test_noalloc_equals_workspace_entry_point_on_two_calls():
@@ -64,12 +77,26 @@ def test_noalloc_equals_workspace_entry_point_on_two_calls():
     cases = [(65536, 3, 256, 64), (131072, 4, 128, 16)]  # 196,608 then 524,288 routes
     for tokens, k, experts, block in cases:
         ids = torch.from_numpy(rng.integers(0, experts, (tokens, k), dtype=np.int32)).to(DEV)
-        ref = with_workspace(ids, experts, block)
-        got = without_allocation(ids, experts, block)
-        torch.cuda.synchronize(DEV)
-        for r, g in zip(ref, got):
-            assert torch.equal(r, g)
-        assert int(got[2].item()) >= ids.numel()
+        assert int(L.lib().exf_moe_align_workspace_bytes(ids.numel(), experts)) > 0
+        check_equal(ids, experts, block)
+
+
+def test_noalloc_int64_ids_small_input_and_the_exact_limit():
+    torch.cuda.set_device(DEV)
+    rng = np.random.default_rng(20261202)
+    # int64 ids through the scratch path
+    ids = torch.from_numpy(rng.integers(0, 256, (32768, 8), dtype=np.int64)).to(DEV)
+    check_equal(ids, 256, 64)
+    # at most 8192 routes: one CTA, no scratch lookup
+    for dt in (np.int32, np.int64):
+        ids = torch.from_numpy(rng.integers(0, 128, (1024, 8)).astype(dt)).to(DEV)
+        assert int(L.lib().exf_moe_align_workspace_bytes(ids.numel(), 128)) == 0
+        check_equal(ids, 128, 16)
+    # exactly at the limit, 2048 * floor(262144 / experts) routes, is accepted
+    experts = 384
+    numel = 2048 * (262144 // experts)
+    ids = torch.from_numpy(rng.integers(0, experts, numel, dtype=np.int32)).to(DEV)
+    check_equal(ids, experts, 32)
 
 
 def test_noalloc_refuses_inputs_beyond_its_scratch():
