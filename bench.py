@@ -2,16 +2,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Default workload (the 48-layer sharded run): each GPU routes and folds T = 131072 tokens per
-layer through 48 Qwen3-shaped MoE layers (E = 128, top-8, keep P = 4, independent per-layer
+Headline (the 48-layer sharded run): each GPU routes and folds T = 131072 tokens per layer
+through 48 Qwen3-shaped MoE layers (E = 128, top-8, keep P = 4, independent per-layer
 calibration tables), so per-GPU work is fixed as N grows (weak scaling; prefill needs no
 communication).  One step = 48 launches of the fused router + prefill-fold kernel, one per layer
 as a model calls it, replayed from a CUDA graph.  The 3.2 GB of logits per step are larger than
-L2, so no flush is needed between steps.  Rank 0 prints one JSON line.
+L2, so no flush is needed between steps.  `value` counts token-layers per second (tokens routed
+through one layer; a forward pass over all 48 layers is `value` / 48 tokens per second).
 
---impl reference runs the reference's CPU path for the same metric: the CPU oracle (a scalar C
-port of exfold/qwen3/kernels.py with the softmax/top-k router) on all host threads over a
-bounded sample of the same workload; under torchrun only rank 0 works.
+The same line carries the rest of the metric "fold-transform tokens/s & MoE-layer us":
+* `decode`: the decode budget of the 48-layer run (B = 1024 batch-sharded, D = 64, one int64
+  importance all-reduce per layer at N > 1), with `decode_parity` at N > 1 (each rank's sharded
+  result equals the single-GPU decode of the whole batch);
+* `configs` (N = 1): the single-layer configurations -- config 0 (Qwen3 prefill fold, T = 4096),
+  config 1 (Qwen3 decode transform and expert layer, B = 256, D = 64, H = 2048, I = 768),
+  config 2 (DeepSeek-style fold, T = 65536, P = 3, E = 256, and its expert layer, H = 4096,
+  I = 2048), config 3 (DeepSeek-style decode sweep, B in {8, 32, 128, 512} x D in {64, 128},
+  transform and expert layer).  Inputs that fit in L2 are timed one launch at a time with L2
+  flushed (a 512 MiB write) between launches, outside the timed events;
+* `cpu_baseline`: the CPU oracle on every host core over a bounded sample of the 48 layers.
+
+--impl reference runs the reference's CPU path for the same metric and config: the CPU oracle (a
+scalar C port of the reference's fold kernels with the softmax/top-k router) on all host threads,
+each step all 48 layers' tables over T tokens per layer (T = 131072 unless the run would exceed
+about two and a half minutes, then fewer, stated); under torchrun only rank 0 works.
 """
 
 from __future__ import annotations
@@ -34,6 +48,8 @@ for _p in (ROOT, ROOT / "exfold-moe_b200"):
 import numpy as np  # noqa: E402
 
 LAYERS, TOKENS, EXPERTS, TOP_K, KEEP = 48, 131072, 128, 8, 4
+METRIC = "fold-transform token-layers/s (router + prefill fold, 48 layers, T=131072/GPU, P=4)"
+UNIT = "token-layers/s"
 
 
 def bytes_per_launch(tokens: int) -> int:
@@ -51,8 +67,8 @@ def measured_peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.is_file():
         d = json.loads(path.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def profiled_traffic(name: str):
@@ -62,7 +78,7 @@ def profiled_traffic(name: str):
     return None
 
 
-# ---- clocks sampled during the timed region (NVML; read-only) ---------------------------------
+# ---- clocks sampled during the timed regions (NVML; read-only) ------------------------------
 _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
             0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
             0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
@@ -70,9 +86,10 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_
 
 
 class ClockSampler:
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
+        self.period_s = period_s
         self._stop = threading.Event()
         self._h = None
         try:
@@ -102,7 +119,7 @@ class ClockSampler:
                 self.samples.append((mhz, reasons))
             except Exception:  # noqa: BLE001
                 pass
-            time.sleep(0.02)
+            time.sleep(self.period_s)
 
     def __enter__(self):
         if self._h is not None:
@@ -144,26 +161,27 @@ def qwen3_tables(layers: int):
                                      validate=False)
 
 
-def cpu_oracle_rate(logits: np.ndarray, coeff: np.ndarray, loss: np.ndarray, threads: int,
-                    budget_s: float) -> tuple[float, int]:
-    """Tokens/s of the CPU oracle (router + fold) on `threads` host threads; ctypes releases the
-    GIL, so threads run the C code in parallel.  Repeats the sample until budget_s is spent."""
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def cpu_layers_pass(pool: ThreadPoolExecutor, threads: int, logits: list, coeff, loss) -> int:
+    """One pass of the CPU oracle's router + Qwen3 fold over layers 0..len(logits)-1 (layer l:
+    logits[l] with tables coeff[l], loss[l]), each layer's tokens split over `threads` host
+    threads (ctypes releases the GIL, so the C code runs in parallel).  Returns token-layers."""
     from oracle import oracle as O
 
-    chunks = np.array_split(np.arange(logits.shape[0]), threads)
+    def work(job):
+        x, c, l_ = job
+        O.router_fold(x, TOP_K, KEEP, c, l_)
 
-    def work(idx):
-        O.router_fold(logits[idx], TOP_K, KEEP, coeff, loss)
-
-    done = 0
-    t0 = time.perf_counter()
-    with ThreadPoolExecutor(max_workers=threads) as ex:
-        while True:
-            list(ex.map(work, chunks))
-            done += logits.shape[0]
-            if time.perf_counter() - t0 >= budget_s:
-                break
-    return done / (time.perf_counter() - t0), done
+    jobs = []
+    for layer, x in enumerate(logits):
+        bounds = np.linspace(0, x.shape[0], threads + 1).astype(int)
+        jobs += [(x[a:b], coeff[layer], loss[layer]) for a, b in zip(bounds[:-1], bounds[1:])
+                 if b > a]
+    list(pool.map(work, jobs))
+    return sum(x.shape[0] for x in logits)
 
 
 def run_reference(args) -> None:
@@ -172,39 +190,102 @@ def run_reference(args) -> None:
         return
     from exfold_b200 import workloads as W
 
-    threads = len(os.sched_getaffinity(0))
-    coeff, loss, _ = qwen3_tables(1)
-    sample = W.logits(W.WORKLOADS["qwen3_layers"]["seed"], 16384, EXPERTS)
-    rate, _ = cpu_oracle_rate(sample, coeff[0], loss[0], threads, 1.0)  # warm-up
-    # whole run bounded to ~2 minutes: at most 0.25 s of CPU work per step
-    step_s = min(0.25, 120.0 / (args.steps + args.warmup))
-    step_tokens = max(threads * 64, int(rate * step_s))
-    step_tokens = min(step_tokens, sample.shape[0])
-    sample = sample[:step_tokens]
-    times = []
-    for i in range(args.warmup + args.steps):
+    threads = host_threads()
+    coeff, loss, _ = qwen3_tables(LAYERS)
+    full = W.logits(W.WORKLOADS["qwen3_layers"]["seed"], TOKENS, EXPERTS)
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        # calibrate on 4096 tokens of every layer, then size the step so that the whole run
+        # stays within about 150 s
         t0 = time.perf_counter()
-        cpu_oracle_rate(sample, coeff[0], loss[0], threads, 0.0)
-        if i >= args.warmup:
-            times.append(time.perf_counter() - t0)
+        done = cpu_layers_pass(pool, threads, [full[:4096]] * LAYERS, coeff, loss)
+        rate = done / (time.perf_counter() - t0)
+        budget_s = 150.0 / (args.steps + args.warmup)
+        tokens = int(min(TOKENS, max(threads * 16, rate * budget_s / LAYERS)))
+        step_logits = [full[:tokens]] * LAYERS
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            cpu_layers_pass(pool, threads, step_logits, coeff, loss)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = step_tokens * len(times) / total
+    value = tokens * LAYERS * len(times) / total
+    sample = (f"{tokens} tokens x all {LAYERS} layers' tables per step (the full workload is "
+              f"{TOKENS} tokens per layer), one seeded {TOKENS}-token logit matrix shared by "
+              f"the layers, split over {threads} threads")
     line = {
-        "metric": "fold-transform tokens/s (router + prefill fold, 48 layers, T=131072/GPU, P=4)",
-        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
         "data": "synthetic (seeded N(0,1) logits, seeded calibration tables)",
         "config": {"workload": "qwen3_layers_prefill", "layers": LAYERS, "tokens_per_gpu": TOKENS,
                    "experts": EXPERTS, "top_k": TOP_K, "keep": KEEP,
-                   "sample_tokens_per_step": step_tokens},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{step_tokens} tokens of layer 0 per step, split over "
-                                   f"{threads} threads"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+                   "sample_tokens_per_layer": tokens, "same_config": tokens == TOKENS},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ---- timing helpers --------------------------------------------------------------------------
+class Timer:
+    """CUDA-event timing on one stream: `graph(fn)` captures fn into a CUDA graph; `replays`
+    times back-to-back replays (inputs larger than L2); `flushed` times single replays with L2
+    flushed between them (a 512 MiB write outside the timed events) for inputs that fit in L2."""
+
+    def __init__(self, dev, stream, warmup: int):
+        import torch
+
+        self.torch, self.dev, self.stream, self.warmup = torch, dev, stream, warmup
+        self._flush = None
+
+    def graph(self, fn):
+        torch = self.torch
+        with torch.cuda.stream(self.stream):
+            fn()
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                fn()
+        return g
+
+    def replays(self, fn, steps: int) -> float:
+        """ms per call, `steps` back-to-back graph replays."""
+        torch = self.torch
+        g = self.graph(fn)
+        with torch.cuda.stream(self.stream):
+            for _ in range(self.warmup):
+                g.replay()
+            torch.cuda.synchronize(self.dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(self.stream)
+            for _ in range(steps):
+                g.replay()
+            b.record(self.stream)
+            torch.cuda.synchronize(self.dev)
+        del g
+        return a.elapsed_time(b) / steps
+
+    def flushed(self, fn, steps: int) -> float:
+        """median ms of single graph replays, L2 flushed before each (outside the events)."""
+        torch = self.torch
+        if self._flush is None:
+            self._flush = torch.empty(1 << 29, dtype=torch.uint8, device=self.dev)
+        g = self.graph(fn)
+        times = []
+        with torch.cuda.stream(self.stream):
+            for i in range(self.warmup + steps):
+                self._flush.fill_(i & 0xFF)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(self.stream)
+                g.replay()
+                b.record(self.stream)
+                b.synchronize()
+                if i >= self.warmup:
+                    times.append(a.elapsed_time(b))
+        del g
+        return statistics.median(times)
 
 
 # ---- decode half of the 48-layer workload -----------------------------------------------------
@@ -214,7 +295,9 @@ DECODE_BATCH, DECODE_BUDGET = 1024, 64
 def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
     """Decode budget over all layers for a B=1024 batch split over the ranks: per layer one
     fixed-point importance launch, one int64 all-reduce of E values, one select/apply launch
-    (a single fused launch on one GPU).  Replayed from a CUDA graph; microseconds per layer."""
+    (a single fused launch on one GPU).  Replayed from a CUDA graph; microseconds per layer.
+    At N > 1, each rank's sharded result of every layer is compared with the single-GPU decode
+    of the whole batch (every rank generates the whole batch from the same seed)."""
     import torch
     import torch.distributed as dist
 
@@ -233,30 +316,264 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
         ids[layer].copy_(li)
     imp = torch.zeros((LAYERS, EXPERTS), dtype=torch.int64, device=dev)
 
-    def step():
+    def step(outs: list):
         for layer in range(LAYERS):
             if world == 1:
-                ops.decode(w[layer], ids[layer], norms[layer], coeff[layer], loss[layer],
-                           DECODE_BUDGET, variant="qwen3")
+                dw, di = ops.decode(w[layer], ids[layer], norms[layer], coeff[layer], loss[layer],
+                                    DECODE_BUDGET, variant="qwen3")
             else:
                 imp[layer].zero_()
                 ops.decode_importance(w[layer], ids[layer], norms[layer], imp[layer])
                 dist.all_reduce(imp[layer])
-                ops.decode_apply(imp[layer], w[layer], ids[layer], coeff[layer], loss[layer],
-                                 DECODE_BUDGET, variant="qwen3")
+                dw, di = ops.decode_apply(imp[layer], w[layer], ids[layer], coeff[layer],
+                                          loss[layer], DECODE_BUDGET, variant="qwen3")
+            outs.append((dw, di))
 
-    step()
+    step([])
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
+    results: list = []  # the graph's output tensors: each replay rewrites them
     with torch.cuda.graph(graph, stream=stream):
-        step()
+        step(results)
     steps = max(10, args.steps // 10)
     ms = timed(graph.replay, steps) / steps
+    out = {"workload": "qwen3_layers_decode", "batch": DECODE_BATCH,
+           "batch_per_gpu": end - start, "budget": DECODE_BUDGET, "layers": LAYERS,
+           "us_per_layer": 1e3 * ms / LAYERS, "scaling": "strong (B fixed)",
+           "launches_per_layer": 1 if world == 1 else 3,
+           "collective": None if world == 1 else "all_reduce int64[128] per layer (NCCL)"}
+    if world > 1:
+        # the last replay's outputs against the single-GPU decode of the whole batch
+        with torch.cuda.stream(stream):
+            graph.replay()
+            same = True
+            for layer in range(LAYERS):
+                fw, fi = ops.router_topk(logits[layer], TOP_K)
+                ew, ei = ops.decode(fw, fi, norms[layer], coeff[layer], loss[layer],
+                                    DECODE_BUDGET, variant="qwen3")
+                gw, gi = results[layer]
+                same = same and bool(torch.equal(ei[start:end], gi)) and bool(
+                    torch.equal(ew[start:end], gw))
+        flag = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        out["decode_parity"] = bool(flag.item())
     del graph
-    return {"workload": "qwen3_layers_decode", "batch": DECODE_BATCH, "batch_per_gpu": end - start,
-            "budget": DECODE_BUDGET, "layers": LAYERS, "us_per_layer": 1e3 * ms / LAYERS,
-            "launches_per_layer": 1 if world == 1 else 3,
-            "collective": None if world == 1 else "all_reduce int64[128] per layer (NCCL)"}
+    return out
+
+
+# ---- the single-layer configurations (N = 1) --------------------------------------------------
+def _dsv4_tables(lay, dev):
+    import torch
+
+    coeff, loss = lay.coeff.copy(), lay.loss.copy()
+    np.fill_diagonal(coeff, 1.0)
+    np.fill_diagonal(loss, 1e30)
+    conf = loss.copy()
+    np.fill_diagonal(conf, 0.0)
+    return tuple(torch.from_numpy(a).to(dev) for a in (coeff, loss, conf))
+
+
+def _qwen3_tables(lay, dev):
+    import torch
+
+    from exfold_b200 import calibration
+
+    c, l_, n = calibration.prepare_qwen3(lay.coeff[None], lay.loss[None], lay.norms[None],
+                                         validate=False)
+    return tuple(torch.from_numpy(np.ascontiguousarray(a[0])).to(dev) for a in (c, l_, n))
+
+
+def _expert_weights(experts, hidden, inter, seed, dev):
+    """bf16 SwiGLU expert weights ~ N(0, 0.02), generated per expert to bound temporaries."""
+    import torch
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    w13 = torch.empty(experts, 2 * inter, hidden, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(experts, hidden, inter, dtype=torch.bfloat16, device=dev)
+    for e in range(experts):
+        w13[e] = 0.02 * torch.randn(2 * inter, hidden, generator=gen, device=dev)
+        w2[e] = 0.02 * torch.randn(hidden, inter, generator=gen, device=dev)
+    return w13, w2
+
+
+def _hbm(nbytes, ms, peaks):
+    gbs = nbytes / ms / 1e6
+    return {"bytes": int(nbytes), "gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
+
+
+def config0(t: Timer, dev, peaks, steps) -> dict:
+    """Qwen3 prefill fold, T=4096, E=128, top-8, P=4: one fused router + fold launch."""
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    lay = W.layer("qwen3_prefill")
+    c, l_, _ = _qwen3_tables(lay, dev)
+    x = torch.from_numpy(lay.logits).to(dev)
+    ow = torch.empty((lay.tokens, KEEP), device=dev)
+    oi = torch.empty((lay.tokens, KEEP), dtype=torch.int32, device=dev)
+    ms = t.flushed(lambda: ops.router_fold_prefill(x, TOP_K, KEEP, c, l_, out=(ow, oi)), steps)
+    nbytes = lay.tokens * (128 * 4 + KEEP * 8) + 2 * 128 * 128 * 4
+    return {"tokens": lay.tokens, "us": ms * 1e3, "tokens_per_s": lay.tokens / ms * 1e3,
+            "l2": "flushed between launches", "launches": 1, **_hbm(nbytes, ms, peaks)}
+
+
+def config1(t: Timer, dev, peaks, steps) -> dict:
+    """Qwen3 decode, B=256, E=128, D=64: the transform (router + decode budget) and the expert
+    layer (H=2048, I=768): the layer alone, the decode fused with the layer, and the whole step
+    (router + fused decode and layer)."""
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    cfg = W.WORKLOADS["qwen3_decode"]
+    lay = W.layer("qwen3_decode")
+    c, l_, n = _qwen3_tables(lay, dev)
+    x_logits = torch.from_numpy(lay.logits).to(dev)
+    hidden, inter, budget = cfg["hidden"], cfg["intermediate"], cfg["budget"]
+
+    def transform():
+        rw, ri = ops.router_topk(x_logits, TOP_K)
+        return ops.decode(rw, ri, n, c, l_, budget, variant="qwen3")
+
+    us_transform = t.flushed(transform, steps) * 1e3
+    tbytes = lay.tokens * 128 * 4 + 2 * 128 * 128 * 4 + 128 * 4 + lay.tokens * TOP_K * 8
+    w13, w2 = _expert_weights(128, hidden, inter, 111, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(112)
+    x = torch.randn(lay.tokens, hidden, generator=gen, device=dev).to(torch.bfloat16)
+    rw, ri = ops.router_topk(x_logits, TOP_K)
+    dw, di = ops.decode(rw, ri, n, c, l_, budget, variant="qwen3")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ms_layer = t.replays(lambda: ops.fused_experts(x, dw, di, w13, w2, status=status), steps)
+    ms_fused = t.replays(lambda: ops.decode_fused_experts(
+        x, rw, ri, n, c, l_, budget, w13, w2, variant="qwen3", status=status), steps)
+
+    def whole():
+        a, b = ops.router_topk(x_logits, TOP_K)
+        ops.decode_fused_experts(x, a, b, n, c, l_, budget, w13, w2, variant="qwen3",
+                                 status=status)
+
+    ms_step = t.replays(whole, steps)
+    active = int(torch.unique(di).numel())
+    wbytes = active * 3 * hidden * inter * 2
+    torch.cuda.synchronize(dev)
+    out = {"batch": lay.tokens, "budget": budget, "hidden": hidden, "inter": inter,
+           "transform_us": us_transform, "transform": _hbm(tbytes, us_transform / 1e3, peaks),
+           "active_experts": active, "moe_layer_us": ms_layer * 1e3,
+           "moe_layer_weights": _hbm(wbytes, ms_layer, peaks),
+           "decode_fused_layer_us": ms_fused * 1e3,
+           "step_us_router_decode_layer": ms_step * 1e3, "status": int(status.item()),
+           "l2": "transform flushed between launches; expert weights > L2"}
+    del w13, w2
+    return out
+
+
+def config2(t: Timer, dev, peaks, steps, weights) -> dict:
+    """DeepSeek-style prefill: biased-sigmoid router + DeepSeek-V4 fold (P=3, similarity blend)
+    over T=65536 tokens and E=256 in one launch, then the expert layer (H=4096, I=2048)."""
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    lay = W.layer("dsv4_prefill")
+    c, l_, cf = _dsv4_tables(lay, dev)
+    x_logits = torch.from_numpy(lay.logits).to(dev)
+    b = torch.from_numpy(lay.bias).to(dev)
+    ow = torch.empty((lay.tokens, 3), device=dev)
+    oi = torch.empty((lay.tokens, 3), dtype=torch.int32, device=dev)
+
+    def fold():
+        ops.router_fold_prefill(x_logits, 8, 3, c, l_, scoring="sigmoid", bias=b,
+                                variant="dsv4", renorm_mode=2, conf_loss=cf, out=(ow, oi))
+
+    ms_fold = t.flushed(fold, steps)
+    fbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
+    w13, w2 = weights
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(212)
+    x = torch.randn(lay.tokens, 4096, generator=gen, device=dev).to(torch.bfloat16)
+    fold()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ms_layer = t.replays(lambda: ops.fused_experts(x, ow, oi, w13, w2, status=status),
+                         max(3, steps // 4))
+    flops = 6.0 * oi.numel() * 4096 * 2048
+    tflops = flops / ms_layer / 1e9
+    out = {"tokens": lay.tokens, "keep": 3, "renorm": "similarity_blend",
+           "fold_us": ms_fold * 1e3, "fold_tokens_per_s": lay.tokens / ms_fold * 1e3,
+           "fold": _hbm(fbytes, ms_fold, peaks), "fold_l2": "flushed between launches",
+           "active_experts": int(torch.unique(oi).numel()), "routes": oi.numel(),
+           "moe_layer_ms": ms_layer,
+           "moe_layer_tensor": {"tflops": tflops, "peak": peaks["bf16_tflops"],
+                                "frac": tflops / peaks["bf16_tflops"], "flops": flops},
+           "status": int(status.item())}
+    del x
+    return out
+
+
+def config3(t: Timer, dev, peaks, steps, weights) -> list:
+    """DeepSeek-style decode sweep, E=256: per (B, D) the transform (biased router + decode
+    budget) and the step with the expert layer (router + decode fused with moe_align, gather,
+    GEMMs and combine; H=4096, I=2048)."""
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    cfg = W.WORKLOADS["dsv4_decode"]
+    w13, w2 = weights
+    rows = []
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(313)
+    for batch in cfg["batches"]:
+        lay = W.Layer(seed=cfg["seed"], tokens=batch, experts=256, top_k=8, kind="dsv4")
+        c, l_, _ = _dsv4_tables(lay, dev)
+        n = torch.from_numpy(lay.norms).to(dev)
+        xl = torch.from_numpy(lay.logits).to(dev)
+        b = torch.from_numpy(lay.bias).to(dev)
+        x = torch.randn(batch, 4096, generator=gen, device=dev).to(torch.bfloat16)
+        for budget in cfg["budgets"]:
+            def transform():
+                rw, ri = ops.router_topk(xl, 8, "sigmoid", b)
+                ops.decode(rw, ri, n, c, l_, budget, variant="dsv4")
+
+            def step():
+                rw, ri = ops.router_topk(xl, 8, "sigmoid", b)
+                ops.decode_fused_experts(x, rw, ri, n, c, l_, budget, w13, w2, variant="dsv4",
+                                         status=status)
+
+            us_t = t.flushed(transform, steps) * 1e3
+            ms_s = t.replays(step, steps)
+            rw, ri = ops.router_topk(xl, 8, "sigmoid", b)
+            _, di = ops.decode(rw, ri, n, c, l_, budget, variant="dsv4")
+            active = int(torch.unique(di).numel())
+            tbytes = batch * 256 * 4 + 2 * 256 * 256 * 4 + 256 * 4 + batch * 8 * 8
+            wbytes = active * 3 * 4096 * 2048 * 2
+            rows.append({"batch": batch, "budget": budget, "transform_us": us_t,
+                         "transform_gbs": tbytes / us_t / 1e3, "active_experts": active,
+                         "step_us_router_decode_layer": ms_s * 1e3,
+                         "layer_weights": _hbm(wbytes, ms_s, peaks)})
+    torch.cuda.synchronize(dev)
+    if int(status.item()) != 0:
+        rows.append({"status": int(status.item())})
+    return rows
+
+
+def measure_configs(dev, stream, peaks, args) -> dict:
+    t = Timer(dev, stream, max(3, args.warmup))
+    steps = max(10, min(args.steps, 50))
+    out = {"config0_qwen3_prefill_fold": config0(t, dev, peaks, steps),
+           "config1_qwen3_decode": config1(t, dev, peaks, steps)}
+    weights = _expert_weights(256, 4096, 2048, 222, dev)
+    out["config2_dsv4_prefill"] = config2(t, dev, peaks, steps, weights)
+    out["config3_dsv4_decode_sweep"] = config3(t, dev, peaks, steps, weights)
+    del weights
+    return out
 
 
 # ---- our arm --------------------------------------------------------------------------------
@@ -322,95 +639,110 @@ def run_ours(args) -> None:
             ms = float(t.item())
         return ms
 
-    with torch.cuda.stream(stream):
-        with ClockSampler(local) as clocks:
-            ms = timed(graph.replay, args.steps)
-    ms_per_step = ms / args.steps
-    tokens_per_step = LAYERS * TOKENS * world
-    value = tokens_per_step / (ms_per_step / 1e3)
-    launch_s = ms_per_step / 1e3 / LAYERS
     peaks = measured_peaks()
-    achieved = bytes_per_launch(TOKENS) / launch_s / 1e9
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            ms = timed(graph.replay, args.steps)
+        ms_per_step = ms / args.steps
+        tokens_per_step = LAYERS * TOKENS * world
+        value = tokens_per_step / (ms_per_step / 1e3)
+        launch_s = ms_per_step / 1e3 / LAYERS
+        achieved = bytes_per_launch(TOKENS) / launch_s / 1e9
 
-    # layer-batched variant: one launch over all 48 layers
-    def batched():
-        ops.router_fold_prefill(logits, TOP_K, KEEP, coeff, loss, out=(out_w, out_ids))
+        # layer-batched variant: one launch over all 48 layers
+        def batched():
+            ops.router_fold_prefill(logits, TOP_K, KEEP, coeff, loss, out=(out_w, out_ids))
 
-    with torch.cuda.stream(stream):
-        batched()
-        torch.cuda.synchronize(dev)
-        gb = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gb, stream=stream):
+        with torch.cuda.stream(stream):
             batched()
-        ms_b = timed(gb.replay, max(1, args.steps // 4)) / max(1, args.steps // 4)
+            torch.cuda.synchronize(dev)
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gb, stream=stream):
+                batched()
+            ms_b = timed(gb.replay, max(1, args.steps // 4)) / max(1, args.steps // 4)
 
-    # end to end through the public API: pinned host logits in, pinned host results out
-    slots = min(4, LAYERS)
-    host_in = torch.empty((slots, TOKENS, EXPERTS), dtype=torch.float32).pin_memory()
-    host_in.copy_(logits[:slots].cpu())
-    host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
-    host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
-    dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.float32, device=dev)
-    dev_w = torch.empty((2, TOKENS, KEEP), dtype=torch.float32, device=dev)
-    dev_i = torch.empty((2, TOKENS, KEEP), dtype=torch.int32, device=dev)
-    # Host->device copies, the router calls and device->host copies on three streams, double
-    # buffered, so that layer l's results go back while layer l+1's logits come in (PCIe runs
-    # both directions at once).  Every copy of the step stays inside the timed region.
-    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]    # logits of buffer b are on the device
-    ev_done = [torch.cuda.Event() for _ in range(2)]  # the call reading buffer b has finished
-    ev_back = [torch.cuda.Event() for _ in range(2)]  # results of buffer b are on the host
+        # end to end through the public API: pinned host logits in, pinned host results out
+        slots = min(4, LAYERS)
+        host_in = torch.empty((slots, TOKENS, EXPERTS), dtype=torch.float32).pin_memory()
+        host_in.copy_(logits[:slots].cpu())
+        host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
+        host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
+        dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.float32, device=dev)
+        dev_w = torch.empty((2, TOKENS, KEEP), dtype=torch.float32, device=dev)
+        dev_i = torch.empty((2, TOKENS, KEEP), dtype=torch.int32, device=dev)
+        # Host->device copies, the router calls and device->host copies on three streams,
+        # double buffered, so that layer l's results go back while layer l+1's logits come in
+        # (PCIe runs both directions at once).  Every copy of the step is inside the timed region.
+        copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_in = [torch.cuda.Event() for _ in range(2)]    # logits of buffer b are on the device
+        ev_done = [torch.cuda.Event() for _ in range(2)]  # the call reading buffer b finished
+        ev_back = [torch.cuda.Event() for _ in range(2)]  # results of buffer b are on the host
 
-    def e2e_step():
-        copy_in.wait_stream(stream)
-        for layer in range(LAYERS):
-            b = layer % 2
-            copy_in.wait_event(ev_done[b])
-            with torch.cuda.stream(copy_in):
-                dev_in[b].copy_(host_in[layer % slots], non_blocking=True)
-            ev_in[b].record(copy_in)
-            stream.wait_event(ev_in[b])
-            stream.wait_event(ev_back[b])
-            ops.router_fold_prefill(dev_in[b], TOP_K, KEEP, coeff[layer], loss[layer],
-                                    out=(dev_w[b], dev_i[b]))
-            ev_done[b].record(stream)
-            copy_out.wait_event(ev_done[b])
-            with torch.cuda.stream(copy_out):
-                host_w[layer % slots].copy_(dev_w[b], non_blocking=True)
-                host_i[layer % slots].copy_(dev_i[b], non_blocking=True)
-            ev_back[b].record(copy_out)
-        stream.wait_stream(copy_out)
+        def e2e_step():
+            copy_in.wait_stream(stream)
+            for layer in range(LAYERS):
+                b = layer % 2
+                copy_in.wait_event(ev_done[b])
+                with torch.cuda.stream(copy_in):
+                    dev_in[b].copy_(host_in[layer % slots], non_blocking=True)
+                ev_in[b].record(copy_in)
+                stream.wait_event(ev_in[b])
+                stream.wait_event(ev_back[b])
+                ops.router_fold_prefill(dev_in[b], TOP_K, KEEP, coeff[layer], loss[layer],
+                                        out=(dev_w[b], dev_i[b]))
+                ev_done[b].record(stream)
+                copy_out.wait_event(ev_done[b])
+                with torch.cuda.stream(copy_out):
+                    host_w[layer % slots].copy_(dev_w[b], non_blocking=True)
+                    host_i[layer % slots].copy_(dev_i[b], non_blocking=True)
+                ev_back[b].record(copy_out)
+            stream.wait_stream(copy_out)
 
-    e2e_steps = max(2, min(10, args.steps // 100))
-    saved_warmup = args.warmup
-    args.warmup = 1
-    with torch.cuda.stream(stream):
-        ms_e2e = timed(e2e_step, e2e_steps) / e2e_steps
-    args.warmup = saved_warmup
-    h2d = LAYERS * TOKENS * EXPERTS * 4
-    d2h = LAYERS * TOKENS * KEEP * 8
+        e2e_steps = max(5, min(20, args.steps // 4))
+        saved_warmup = args.warmup
+        args.warmup = 1
+        with torch.cuda.stream(stream):
+            ms_e2e = timed(e2e_step, e2e_steps) / e2e_steps
+        args.warmup = saved_warmup
+        h2d = LAYERS * TOKENS * EXPERTS * 4
+        d2h = LAYERS * TOKENS * KEEP * 8
+        del host_in, host_w, host_i, dev_in, dev_w, dev_i
 
-    with torch.cuda.stream(stream):
-        decode = measure_decode(dev, world, rank, stream, coeff, loss, timed, args)
+        with torch.cuda.stream(stream):
+            decode = measure_decode(dev, world, rank, stream, coeff, loss, timed, args)
+
+        configs = None
+        if world == 1:
+            configs = measure_configs(dev, stream, peaks, args)
 
     cpu = None
     if rank == 0 and world == 1:
-        sample = logits[0, :8192].cpu().numpy()
-        rate, done = cpu_oracle_rate(sample, coeff_np[0], loss_np[0], 1, 10.0)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port",
-               "sample": f"{done} tokens (8192-token slices of layer 0), single thread, ~10 s"}
+        threads = host_threads()
+        from exfold_b200 import workloads as W
+
+        sample = W.logits(W.WORKLOADS["qwen3_layers"]["seed"], 2048, EXPERTS)
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            cpu_layers_pass(pool, threads, [sample[:256]] * LAYERS, coeff_np, loss_np)
+            done, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < 15.0:
+                done += cpu_layers_pass(pool, threads, [sample] * LAYERS, coeff_np, loss_np)
+            rate = done / (time.perf_counter() - t0)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{done} token-layers: 2048 tokens x all {LAYERS} layers' tables per "
+                         f"pass, ~15 s on {threads} threads"}
 
     if rank == 0:
         line = {
-            "metric": "fold-transform tokens/s (router + prefill fold, 48 layers, T=131072/GPU, P=4)",
-            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,1) logits, seeded calibration tables)",
+            "data": "synthetic (seeded N(0,1) logits, seeded calibration tables; expert "
+                    "weights N(0, 0.02) bf16)",
             "config": {"workload": "qwen3_layers_prefill", "layers": LAYERS,
                        "tokens_per_gpu": TOKENS, "experts": EXPERTS, "top_k": TOP_K,
                        "keep": KEEP, "parallelism": f"token-sharded x{world}",
                        "l2": "inputs 3.2 GB/step per GPU > L2, no flush"},
+            "tokens_per_s_per_forward": value / LAYERS,
             "gpu_launches": LAYERS * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
@@ -419,14 +751,15 @@ def run_ours(args) -> None:
                          "kernel": "exf::router_tpt_kernel<qwen3 fold, P=4>",
                          "bytes_per_launch": bytes_per_launch(TOKENS),
                          "us_per_launch": launch_s * 1e6},
-            "layer_batched": {"ms_per_step": ms_b, "tokens_per_s": tokens_per_step / (ms_b / 1e3),
+            "layer_batched": {"ms_per_step": ms_b, "value": tokens_per_step / (ms_b / 1e3),
                               "launches_per_step": 1},
-            "e2e": {"value": tokens_per_step / (ms_e2e / 1e3), "unit": "tokens/s",
+            "e2e": {"value": tokens_per_step / (ms_e2e / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": ms_e2e},
+                    "ms_per_step": ms_e2e, "steps": e2e_steps},
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "decode": decode,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
     del graph, gb
@@ -434,32 +767,7 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-# ---- additional single-GPU workloads (--workload NAME): one JSON line each --------------------
-def _timed_graph(fn, steps: int, warmup: int, dev) -> float:
-    """ms per call of fn, replayed from a CUDA graph, CUDA events on the capture stream."""
-    import torch
-
-    stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        fn()
-        torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            fn()
-        for _ in range(warmup):
-            graph.replay()
-        torch.cuda.synchronize(dev)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(steps):
-            graph.replay()
-        end.record(stream)
-        torch.cuda.synchronize(dev)
-    ms = start.elapsed_time(end) / steps
-    del graph
-    return ms
-
-
+# ---- single workloads (--workload NAME), for profiling: one JSON line each -------------------
 def run_extra(args) -> None:
     import torch
 
@@ -468,141 +776,75 @@ def run_extra(args) -> None:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
-        ROOT / "MEASURED_PEAKS.json").is_file() else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(11)
+    stream = torch.cuda.Stream(dev)
+    peaks = measured_peaks()
+    t = Timer(dev, stream, max(3, args.warmup))
     steps = max(5, min(args.steps, 200))
     out = {"workload": args.workload}
-    if args.workload in ("moe_dsv4_prefill", "moe_qwen3_decode"):
-        if args.workload == "moe_dsv4_prefill":
-            # --tokens / --experts shrink the case for profiling (defaults: the full workload)
-            lay = W.layer("dsv4_prefill", tokens=args.tokens)
-            tokens, experts, hidden, inter = lay.tokens, 256, 4096, 2048
-            coeff, loss = lay.coeff.copy(), lay.loss.copy()
-            np.fill_diagonal(coeff, 1.0)
-            np.fill_diagonal(loss, 1e30)
-            conf = loss.copy()
-            np.fill_diagonal(conf, 0.0)
-            w, ids = ops.router_fold_prefill(
-                torch.from_numpy(lay.logits).to(dev), 8, 3, torch.from_numpy(coeff).to(dev),
-                torch.from_numpy(loss).to(dev), scoring="sigmoid",
-                bias=torch.from_numpy(lay.bias).to(dev), variant="dsv4", renorm_mode=2,
-                conf_loss=torch.from_numpy(conf).to(dev))
-        else:
-            lay = W.layer("qwen3_decode")
-            tokens, experts, hidden, inter = lay.tokens, 128, 2048, 768
-            rw, ri = ops.router_topk(torch.from_numpy(lay.logits).to(dev), 8)
-            w, ids = ops.decode(rw, ri, torch.from_numpy(lay.norms).to(dev),
-                                torch.from_numpy(lay.coeff).to(dev),
-                                torch.from_numpy(lay.loss).to(dev), 64, variant="qwen3")
-        if args.experts and args.experts < experts:  # profiling: fold the routes onto fewer experts
+    if args.workload == "config0":
+        out.update(config0(t, dev, peaks, steps))
+    elif args.workload == "config1":
+        out.update(config1(t, dev, peaks, steps))
+    elif args.workload in ("config2", "config3"):
+        weights = _expert_weights(256, 4096, 2048, 222, dev)
+        fn = config2 if args.workload == "config2" else config3
+        out["result"] = fn(t, dev, peaks, steps, weights)
+    elif args.workload == "moe_dsv4_prefill":
+        # the expert layer alone; --tokens / --experts shrink the case for profiling
+        lay = W.layer("dsv4_prefill", tokens=args.tokens)
+        c, l_, cf = _dsv4_tables(lay, dev)
+        w, ids = ops.router_fold_prefill(
+            torch.from_numpy(lay.logits).to(dev), 8, 3, c, l_, scoring="sigmoid",
+            bias=torch.from_numpy(lay.bias).to(dev), variant="dsv4", renorm_mode=2,
+            conf_loss=cf)
+        experts = 256
+        if args.experts and args.experts < experts:  # fold the routes onto fewer experts
             ids = (ids % args.experts).to(ids.dtype)
             experts = args.experts
-        x = torch.randn(tokens, hidden, generator=gen, device=dev).to(torch.bfloat16)
-        w13 = torch.empty(experts, 2 * inter, hidden, dtype=torch.bfloat16, device=dev)
-        w2 = torch.empty(experts, hidden, inter, dtype=torch.bfloat16, device=dev)
-        for e in range(experts):  # N(0, 0.02) weights, generated per expert to bound memory
-            w13[e] = (0.02 * torch.randn(2 * inter, hidden, generator=gen, device=dev))
-            w2[e] = (0.02 * torch.randn(hidden, inter, generator=gen, device=dev))
+        w13, w2 = _expert_weights(experts, 4096, 2048, 222, dev)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(11)
+        x = torch.randn(lay.tokens, 4096, generator=gen, device=dev).to(torch.bfloat16)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        ms = _timed_graph(lambda: ops.fused_experts(x, w, ids, w13, w2, status=status), steps,
-                          max(3, args.warmup), dev)
-        numel = ids.numel()
-        active = int(torch.unique(ids).numel())
-        flops = 6.0 * numel * hidden * inter
-        wbytes = active * 3.0 * hidden * inter * 2
-        out.update(tokens=tokens, routes=numel, active_experts=active, hidden=hidden, inter=inter,
-                   ms_per_layer=ms, tflops=flops / ms / 1e9,
+        ms = t.replays(lambda: ops.fused_experts(x, w, ids, w13, w2, status=status), steps)
+        flops = 6.0 * ids.numel() * 4096 * 2048
+        out.update(tokens=lay.tokens, routes=ids.numel(), ms_per_layer=ms,
+                   tflops=flops / ms / 1e9,
                    tensor_frac_of_measured_peak=flops / ms / 1e9 / peaks["bf16_tflops"],
-                   weight_gbs=wbytes / ms / 1e6,
-                   hbm_frac_of_measured_peak=wbytes / ms / 1e6 / peaks["hbm_gbs"],
-                   status=int(status.item()), launches=7)
-        if args.workload == "moe_qwen3_decode" and not args.experts:
-            # the decode budget and the expert layer: two calls, and the fused entry (moe_align
-            # inside the decode launch, duplicate (token, expert) routes merged)
-            n, c, l_ = (torch.from_numpy(a).to(dev) for a in (lay.norms, lay.coeff, lay.loss))
-
-            def two_calls():
-                dw, di = ops.decode(rw, ri, n, c, l_, 64, variant="qwen3")
-                ops.fused_experts(x, dw, di, w13, w2, status=status)
-
-            def fused():
-                ops.decode_fused_experts(x, rw, ri, n, c, l_, 64, w13, w2, variant="qwen3",
-                                         status=status)
-
-            ms_two = _timed_graph(two_calls, steps, max(3, args.warmup), dev)
-            ms_fused = _timed_graph(fused, steps, max(3, args.warmup), dev)
-            merged = int((ids.sort(dim=1).values.diff(dim=1) == 0).sum().item())
-            out["decode_layer"] = {"us_decode_then_experts": ms_two * 1e3,
-                                   "us_decode_fused_experts": ms_fused * 1e3,
-                                   "merged_routes": merged, "status": int(status.item())}
-    elif args.workload == "dsv4_prefill_fold":
-        lay = W.layer("dsv4_prefill")
-        coeff, loss = lay.coeff.copy(), lay.loss.copy()
-        np.fill_diagonal(coeff, 1.0)
-        np.fill_diagonal(loss, 1e30)
-        conf = loss.copy()
-        np.fill_diagonal(conf, 0.0)
-        xs = torch.from_numpy(lay.logits).to(dev)
-        c, l_, cf = (torch.from_numpy(a).to(dev) for a in (coeff, loss, conf))
-        b = torch.from_numpy(lay.bias).to(dev)
-        ow = torch.empty((lay.tokens, 3), device=dev)
-        oi = torch.empty((lay.tokens, 3), dtype=torch.int32, device=dev)
-        ms = _timed_graph(lambda: ops.router_fold_prefill(
-            xs, 8, 3, c, l_, scoring="sigmoid", bias=b, variant="dsv4", renorm_mode=2,
-            conf_loss=cf, out=(ow, oi)), steps, max(3, args.warmup), dev)
-        nbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
-        out.update(tokens=lay.tokens, us_per_launch=ms * 1e3, tokens_per_s=lay.tokens / ms * 1e3,
-                   gbs=nbytes / ms / 1e6, hbm_frac_of_measured_peak=nbytes / ms / 1e6 / peaks["hbm_gbs"])
+                   status=int(status.item()))
+    elif args.workload == "moe_qwen3_decode":
+        out.update(config1(t, dev, peaks, steps))
     elif args.workload == "calibration_update":
         # PairwiseScalarStats.update (exfold/qwen3/calibration.py:49-95) at the Qwen3 layer shape:
         # 8 routes of 2048-wide bf16 expert outputs over 128 experts, 16384 tokens per call
         # (512 MiB of outputs > L2); the pass is bound by reading the outputs.
         from exfold_b200.calibration import PairwiseScalarStats
 
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(11)
         T, K, H, E = (args.tokens or 16384), 8, 2048, 128
         outs = torch.randn((T, K, H), generator=gen, device=dev).to(torch.bfloat16)
         ids = torch.randint(0, E, (T, K), generator=gen, device=dev, dtype=torch.int32)
         stats = PairwiseScalarStats(E, device=dev)
-        ms = _timed_graph(lambda: stats.update(ids, outs), steps, max(3, args.warmup), dev)
+        ms = t.replays(lambda: stats.update(ids, outs), steps)
         nbytes = T * K * H * 2 + T * K * 4
         out.update(tokens=T, top_k=K, hidden=H, experts=E, us_per_call=ms * 1e3,
-                   tokens_per_s=T / ms * 1e3, gbs=nbytes / ms / 1e6,
-                   hbm_frac_of_measured_peak=nbytes / ms / 1e6 / peaks["hbm_gbs"])
-    elif args.workload == "dsv4_decode":
-        cfg = W.WORKLOADS["dsv4_decode"]
-        rows = []
-        for batch in cfg["batches"]:
-            lay = W.Layer(seed=cfg["seed"], tokens=batch, experts=256, top_k=8, kind="dsv4")
-            coeff, loss = lay.coeff.copy(), lay.loss.copy()
-            np.fill_diagonal(coeff, 1.0)
-            np.fill_diagonal(loss, 1e30)
-            xs = torch.from_numpy(lay.logits).to(dev)
-            b = torch.from_numpy(lay.bias).to(dev)
-            c, l_, n = (torch.from_numpy(a).to(dev) for a in (coeff, loss, lay.norms))
-            for budget in cfg["budgets"]:
-                def step():
-                    rw, ri = ops.router_topk(xs, 8, "sigmoid", b)
-                    ops.decode(rw, ri, n, c, l_, budget, variant="dsv4")
-                ms = _timed_graph(step, steps, max(3, args.warmup), dev)
-                rows.append({"batch": batch, "budget": budget, "us_router_plus_decode": ms * 1e3})
-        out["sweep"] = rows
+                   tokens_per_s=T / ms * 1e3, **_hbm(nbytes, ms, peaks))
     print(json.dumps(out), flush=True)
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller cases for profiling")
     ap.add_argument("--tokens", type=int, default=None, help="smaller cases for profiling")
     ap.add_argument("--experts", type=int, default=0, help="fewer experts (profiling cases)")
     ap.add_argument("--workload", default="qwen3_layers",
-                    choices=["qwen3_layers", "moe_dsv4_prefill", "moe_qwen3_decode",
-                             "dsv4_prefill_fold", "dsv4_decode", "calibration_update"])
+                    choices=["qwen3_layers", "config0", "config1", "config2", "config3",
+                             "moe_dsv4_prefill", "moe_qwen3_decode", "calibration_update"])
     args = ap.parse_args()
     set_shape(args.layers, args.tokens or TOKENS)
     if args.warmup < 3:
