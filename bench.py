@@ -11,9 +11,10 @@ L2, so no flush is needed between steps.  `value` counts token-layers per second
 through one layer; a forward pass over all 48 layers is `value` / 48 tokens per second).
 
 The same line carries the rest of the metric "fold-transform tokens/s & MoE-layer us":
-* `decode`: the decode budget of the 48-layer run (B = 1024 batch-sharded, D = 64, one int64
-  importance all-reduce per layer at N > 1), with `decode_parity` at N > 1 (each rank's sharded
-  result equals the single-GPU decode of the whole batch);
+* `decode`: the decode budget of the 48-layer run (B = 1024 batch-sharded, D = 64; at N > 1 one
+  launch per layer exchanges the int64 importance with the other ranks over NVLink peer memory,
+  and the NCCL all-reduce path is timed beside it), with `decode_parity` at N > 1 (each rank's
+  sharded results, both paths, equal the single-GPU decode of the whole batch);
 * `configs` (N = 1): the single-layer configurations -- config 0 (Qwen3 prefill fold, T = 4096),
   config 1 (Qwen3 decode transform and expert layer, B = 256, D = 64, H = 2048, I = 768),
   config 2 (DeepSeek-style fold, T = 65536, P = 3, E = 256, and its expert layer, H = 4096,
@@ -293,11 +294,13 @@ DECODE_BATCH, DECODE_BUDGET = 1024, 64
 
 
 def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
-    """Decode budget over all layers for a B=1024 batch split over the ranks: per layer one
-    fixed-point importance launch, one int64 all-reduce of E values, one select/apply launch
-    (a single fused launch on one GPU).  Replayed from a CUDA graph; microseconds per layer.
-    At N > 1, each rank's sharded result of every layer is compared with the single-GPU decode
-    of the whole batch (every rank generates the whole batch from the same seed)."""
+    """Decode budget over all layers for a B=1024 batch split over the ranks, replayed from a
+    CUDA graph; microseconds per layer.  One GPU: one fused launch per layer.  N > 1: one launch
+    per layer that exchanges the fixed-point importance with the other ranks over NVLink peer
+    memory (`DecodeExchange`); the three-step path (importance launch, NCCL all-reduce of E
+    int64, apply launch) is timed beside it.  Each rank's results of every layer, both paths,
+    are compared with the single-GPU decode of the whole batch (every rank generates the whole
+    batch from the same seed)."""
     import torch
     import torch.distributed as dist
 
@@ -315,12 +318,15 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
         w[layer].copy_(lw)
         ids[layer].copy_(li)
     imp = torch.zeros((LAYERS, EXPERTS), dtype=torch.int64, device=dev)
+    xch = parallel.DecodeExchange(EXPERTS, device=dev) if world > 1 else None
 
-    def step(outs: list):
+    def step(outs: list, how: str):
         for layer in range(LAYERS):
+            args_ = (w[layer], ids[layer], norms[layer], coeff[layer], loss[layer], DECODE_BUDGET)
             if world == 1:
-                dw, di = ops.decode(w[layer], ids[layer], norms[layer], coeff[layer], loss[layer],
-                                    DECODE_BUDGET, variant="qwen3")
+                dw, di = ops.decode(*args_, variant="qwen3")
+            elif how == "exchange":
+                dw, di = xch.decode(*args_, variant="qwen3")
             else:
                 imp[layer].zero_()
                 ops.decode_importance(w[layer], ids[layer], norms[layer], imp[layer])
@@ -329,35 +335,53 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
                                           loss[layer], DECODE_BUDGET, variant="qwen3")
             outs.append((dw, di))
 
-    step([])
-    torch.cuda.synchronize(dev)
-    graph = torch.cuda.CUDAGraph()
-    results: list = []  # the graph's output tensors: each replay rewrites them
-    with torch.cuda.graph(graph, stream=stream):
-        step(results)
+    def capture(how: str):
+        step([], how)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        results: list = []  # the graph's output tensors: each replay rewrites them
+        with torch.cuda.graph(graph, stream=stream):
+            step(results, how)
+        return graph, results
+
     steps = max(10, args.steps // 10)
+    graph, results = capture("exchange")
     ms = timed(graph.replay, steps) / steps
     out = {"workload": "qwen3_layers_decode", "batch": DECODE_BATCH,
            "batch_per_gpu": end - start, "budget": DECODE_BUDGET, "layers": LAYERS,
            "us_per_layer": 1e3 * ms / LAYERS, "scaling": "strong (B fixed)",
-           "launches_per_layer": 1 if world == 1 else 3,
-           "collective": None if world == 1 else "all_reduce int64[128] per layer (NCCL)"}
+           "launches_per_layer": 1,
+           "collective": None if world == 1 else
+           "in-launch exchange of int64[128] over NVLink peer memory (CUDA IPC)"}
     if world > 1:
-        # the last replay's outputs against the single-GPU decode of the whole batch
+        runs = {"exchange": (graph, results)}
+        graph_nccl, results_nccl = capture("all_reduce")
+        ms_nccl = timed(graph_nccl.replay, steps) / steps
+        runs["all_reduce"] = (graph_nccl, results_nccl)
+        out["all_reduce_path"] = {"us_per_layer": 1e3 * ms_nccl / LAYERS,
+                                  "launches_per_layer": 2,
+                                  "collective": "NCCL all_reduce int64[128] per layer"}
+        same = True
         with torch.cuda.stream(stream):
-            graph.replay()
-            same = True
+            refs = []
             for layer in range(LAYERS):
                 fw, fi = ops.router_topk(logits[layer], TOP_K)
                 ew, ei = ops.decode(fw, fi, norms[layer], coeff[layer], loss[layer],
                                     DECODE_BUDGET, variant="qwen3")
-                gw, gi = results[layer]
-                same = same and bool(torch.equal(ei[start:end], gi)) and bool(
-                    torch.equal(ew[start:end], gw))
+                refs.append((ew[start:end], ei[start:end]))
+            for g, res in runs.values():
+                g.replay()
+                for (gw, gi), (ew, ei) in zip(res, refs):
+                    same = same and bool(torch.equal(ei, gi)) and bool(torch.equal(ew, gw))
+        same = same and int(xch.status.item()) == 0
         flag = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         out["decode_parity"] = bool(flag.item())
-    del graph
+        del runs, graph_nccl, results_nccl
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        xch.close()
+    del graph, results
     return out
 
 
@@ -472,15 +496,16 @@ def config1(t: Timer, dev, peaks, steps) -> dict:
     return out
 
 
-def config2(t: Timer, dev, peaks, steps, weights) -> dict:
-    """DeepSeek-style prefill: biased-sigmoid router + DeepSeek-V4 fold (P=3, similarity blend)
-    over T=65536 tokens and E=256 in one launch, then the expert layer (H=4096, I=2048)."""
+def config2_fold(t: Timer, dev, peaks, steps, tokens=None):
+    """DeepSeek-style prefill fold: biased-sigmoid router + DeepSeek-V4 fold (P=3, similarity
+    blend) over T=65536 tokens (or `tokens`) and E=256 in one launch.  Returns the result and
+    the routes."""
     import torch
 
     from exfold_b200 import ops
     from exfold_b200 import workloads as W
 
-    lay = W.layer("dsv4_prefill")
+    lay = W.layer("dsv4_prefill", tokens=tokens)
     c, l_, cf = _dsv4_tables(lay, dev)
     x_logits = torch.from_numpy(lay.logits).to(dev)
     b = torch.from_numpy(lay.bias).to(dev)
@@ -492,25 +517,37 @@ def config2(t: Timer, dev, peaks, steps, weights) -> dict:
                                 variant="dsv4", renorm_mode=2, conf_loss=cf, out=(ow, oi))
 
     ms_fold = t.flushed(fold, steps)
+    fold()
     fbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
+    out = {"tokens": lay.tokens, "keep": 3, "renorm": "similarity_blend",
+           "fold_us": ms_fold * 1e3, "fold_tokens_per_s": lay.tokens / ms_fold * 1e3,
+           "fold": _hbm(fbytes, ms_fold, peaks), "fold_l2": "flushed between launches"}
+    return out, ow, oi
+
+
+def config2(t: Timer, dev, peaks, steps, weights) -> dict:
+    """DeepSeek-style prefill: the fold (config2_fold), then the expert layer (H=4096, I=2048)
+    over its routes."""
+    import torch
+
+    from exfold_b200 import ops
+
+    out, ow, oi = config2_fold(t, dev, peaks, steps)
+    tokens = ow.shape[0]
     w13, w2 = weights
     gen = torch.Generator(device=dev)
     gen.manual_seed(212)
-    x = torch.randn(lay.tokens, 4096, generator=gen, device=dev).to(torch.bfloat16)
-    fold()
+    x = torch.randn(tokens, 4096, generator=gen, device=dev).to(torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     ms_layer = t.replays(lambda: ops.fused_experts(x, ow, oi, w13, w2, status=status),
                          max(3, steps // 4))
     flops = 6.0 * oi.numel() * 4096 * 2048
     tflops = flops / ms_layer / 1e9
-    out = {"tokens": lay.tokens, "keep": 3, "renorm": "similarity_blend",
-           "fold_us": ms_fold * 1e3, "fold_tokens_per_s": lay.tokens / ms_fold * 1e3,
-           "fold": _hbm(fbytes, ms_fold, peaks), "fold_l2": "flushed between launches",
-           "active_experts": int(torch.unique(oi).numel()), "routes": oi.numel(),
-           "moe_layer_ms": ms_layer,
-           "moe_layer_tensor": {"tflops": tflops, "peak": peaks["bf16_tflops"],
-                                "frac": tflops / peaks["bf16_tflops"], "flops": flops},
-           "status": int(status.item())}
+    out.update({"active_experts": int(torch.unique(oi).numel()), "routes": oi.numel(),
+                "moe_layer_ms": ms_layer,
+                "moe_layer_tensor": {"tflops": tflops, "peak": peaks["bf16_tflops"],
+                                     "frac": tflops / peaks["bf16_tflops"], "flops": flops},
+                "status": int(status.item())})
     del x
     return out
 
@@ -562,6 +599,61 @@ def config3(t: Timer, dev, peaks, steps, weights) -> list:
     if int(status.item()) != 0:
         rows.append({"status": int(status.item())})
     return rows
+
+
+def kernel_workload(name, t: Timer, dev, peaks, steps, tokens=None) -> dict:
+    """One library kernel on a representative input (profiling commands for its summary):
+    fold_kernel: the DeepSeek-V4 fold (mode 2) of given top-8 routes, T=65536, E=256;
+    router_generic: router_kernel, sqrtsoftplus + bias top-8 over E=256 (the DeepSeek-V4
+      model's scoring), T=65536;
+    static_remap: the static decode table and the in-place remap of B=1024 x 8 routes, E=128;
+    moe_align: the chunked moe_align of 196608 routes over 256 experts (block 64) and the
+      one-CTA path on 2048 routes over 128 experts (block 16).
+    The inputs fit in L2; the timings flush it between launches."""
+    import torch
+
+    from exfold_b200 import ops
+    from exfold_b200 import workloads as W
+
+    out: dict = {}
+    if name in ("fold_kernel", "router_generic"):
+        lay = W.layer("dsv4_prefill", tokens=tokens)
+        x = torch.from_numpy(lay.logits).to(dev)
+        b = torch.from_numpy(lay.bias).to(dev)
+        if name == "router_generic":
+            ms = t.flushed(lambda: ops.router_topk(x, 8, "sqrtsoftplus", b), steps)
+            nbytes = lay.tokens * (256 * 4 + 8 * 8) + 256 * 4
+        else:
+            c, l_, cf = _dsv4_tables(lay, dev)
+            w, ids = ops.router_topk(x, 8, "sigmoid", b)
+            ms = t.flushed(lambda: ops.fold_prefill(w, ids, c, l_, 3, variant="dsv4",
+                                                    renorm_mode=2, conf_loss=cf), steps)
+            nbytes = lay.tokens * (8 * 8 + 3 * 8) + 3 * 256 * 256 * 4
+        out.update(tokens=lay.tokens, us=ms * 1e3, **_hbm(nbytes, ms, peaks))
+    elif name == "static_remap":
+        lay = W.layer("qwen3_decode", tokens=1024)
+        c, l_, n = _qwen3_tables(lay, dev)
+        w, ids = ops.router_topk(torch.from_numpy(lay.logits).to(dev), 8)
+        target, scale = ops.static_table(n, c, l_, 64)
+        wc, ic = w.clone(), ids.clone()
+        ms_t = t.flushed(lambda: ops.static_table(n, c, l_, 64), steps)
+        ms_r = t.flushed(lambda: ops.static_remap_(wc, ic, target, scale), steps)
+        out.update(batch=1024, table_us=ms_t * 1e3, remap_us=ms_r * 1e3,
+                   remap=_hbm(2 * w.numel() * 8 + 128 * 8, ms_r, peaks))
+    elif name == "moe_align":
+        big = W.layer("dsv4_prefill", tokens=tokens)
+        _, ids = ops.router_topk(torch.from_numpy(big.logits).to(dev), 8, "sigmoid",
+                                 torch.from_numpy(big.bias).to(dev))
+        ids3 = ids[:, :3].contiguous()
+        ms_big = t.flushed(lambda: ops.moe_align_block_size(ids3, 64, 256), steps)
+        small = W.layer("qwen3_decode")
+        _, ids_s = ops.router_topk(torch.from_numpy(small.logits).to(dev), 8)
+        ms_small = t.flushed(lambda: ops.moe_align_block_size(ids_s, 16, 128), steps)
+        cap = ops.moe_align_capacity(ids3.numel(), 256, 64)
+        out.update(routes=ids3.numel(), chunked_us=ms_big * 1e3,
+                   chunked=_hbm(ids3.numel() * 4 * 2 + cap * 4, ms_big, peaks),
+                   small_routes=ids_s.numel(), small_us=ms_small * 1e3)
+    return out
 
 
 def measure_configs(dev, stream, peaks, args) -> dict:
@@ -698,6 +790,17 @@ def run_ours(args) -> None:
                 ev_back[b].record(copy_out)
             stream.wait_stream(copy_out)
 
+        if args.workload == "prefill_only":  # profiling: the timed prefill step alone
+            if rank == 0:
+                print(json.dumps({"workload": "prefill_only", "layers": LAYERS,
+                                  "tokens": TOKENS, "us_per_launch": launch_s * 1e6,
+                                  "frac": achieved / peaks["hbm_gbs"],
+                                  "batched_us_per_layer": 1e3 * ms_b / LAYERS}), flush=True)
+            del graph, gb
+            if world > 1:
+                dist.destroy_process_group()
+            return
+
         e2e_steps = max(5, min(20, args.steps // 4))
         saved_warmup = args.warmup
         args.warmup = 1
@@ -814,6 +917,10 @@ def run_extra(args) -> None:
                    status=int(status.item()))
     elif args.workload == "moe_qwen3_decode":
         out.update(config1(t, dev, peaks, steps))
+    elif args.workload == "dsv4_fold":
+        out.update(config2_fold(t, dev, peaks, steps, tokens=args.tokens)[0])
+    elif args.workload in ("fold_kernel", "router_generic", "static_remap", "moe_align"):
+        out.update(kernel_workload(args.workload, t, dev, peaks, steps, args.tokens))
     elif args.workload == "calibration_update":
         # PairwiseScalarStats.update (exfold/qwen3/calibration.py:49-95) at the Qwen3 layer shape:
         # 8 routes of 2048-wide bf16 expert outputs over 128 experts, 16384 tokens per call
@@ -843,15 +950,17 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=None, help="smaller cases for profiling")
     ap.add_argument("--experts", type=int, default=0, help="fewer experts (profiling cases)")
     ap.add_argument("--workload", default="qwen3_layers",
-                    choices=["qwen3_layers", "config0", "config1", "config2", "config3",
-                             "moe_dsv4_prefill", "moe_qwen3_decode", "calibration_update"])
+                    choices=["qwen3_layers", "prefill_only", "config0", "config1", "config2",
+                             "config3", "dsv4_fold", "fold_kernel", "router_generic",
+                             "static_remap", "moe_align", "moe_dsv4_prefill",
+                             "moe_qwen3_decode", "calibration_update"])
     args = ap.parse_args()
     set_shape(args.layers, args.tokens or TOKENS)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload != "qwen3_layers":
+    elif args.workload not in ("qwen3_layers", "prefill_only"):
         run_extra(args)
     else:
         run_ours(args)

@@ -1,6 +1,7 @@
 // extern "C" entry points of libexfold_b200.so: argument checks, error reporting, dispatch.
 #include <stdarg.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <atomic>
 #include <mutex>
@@ -234,6 +235,95 @@ EXF_API int exf_decode_apply(const int64_t* importance, const void* w, int w_dty
   EXF_REQUIRE(batch == 0 || (w && ids && out_w && out_ids), "%s: null routing pointer", name);
   DecodeParams p{w, ids, batch * top_k, experts, budget, variant, 1 /*importance given*/,
                  nullptr, importance, nullptr, coeff, loss, out_w, out_ids, out_subset};
+  return cuda_status(launch_decode(w_dtype, id_dtype, p, (cudaStream_t)stream), name);
+}
+
+// ---- sharded decode with the importance exchanged over peer memory ---------------------------
+EXF_API int64_t exf_decode_exchange_bytes(int experts, int world) {
+  if (experts < 1 || experts > 1024 || world < 1 || world > kMaxPeers) return -1;
+  return exchange_longs(experts, world) * (int64_t)sizeof(int64_t);
+}
+
+// cuMemGetAddressRange through the runtime's driver entry point (no link against libcuda)
+typedef int (*exf_get_range_fn)(unsigned long long*, size_t*, unsigned long long);
+
+static cudaError_t allocation_base(const void* ptr, uintptr_t* base) {
+  static exf_get_range_fn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t lookup = cudaSuccess;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    lookup = cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q);
+    if (lookup == cudaSuccess && (q != cudaDriverEntryPointSuccess || f == nullptr))
+      lookup = cudaErrorSymbolNotFound;
+    fn = reinterpret_cast<exf_get_range_fn>(f);
+  });
+  if (lookup != cudaSuccess) return lookup;
+  unsigned long long b = 0;
+  size_t size = 0;
+  if (fn(&b, &size, reinterpret_cast<unsigned long long>(ptr)) != 0)
+    return cudaErrorInvalidDevicePointer;
+  *base = static_cast<uintptr_t>(b);
+  return cudaSuccess;
+}
+
+EXF_API int exf_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  const char* name = "exf_ipc_export";
+  EXF_REQUIRE(ptr && handle && offset, "%s: null pointer", name);
+  uintptr_t base = 0;
+  cudaError_t e = allocation_base(ptr, &base);
+  if (e != cudaSuccess) return cuda_status(e, name);
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_status(e, name);
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - base);
+  return EXF_OK;
+}
+
+EXF_API int exf_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  const char* name = "exf_ipc_import";
+  EXF_REQUIRE(handle && ptr && offset >= 0, "%s: bad argument", name);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, name);
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return EXF_OK;
+}
+
+EXF_API int exf_ipc_release(void* ptr, int64_t offset) {
+  const char* name = "exf_ipc_release";
+  EXF_REQUIRE(ptr && offset >= 0, "%s: bad argument", name);
+  return cuda_status(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset), name);
+}
+
+EXF_API int exf_decode_sharded(const void* w, int w_dtype, const void* ids, int id_dtype,
+                               int64_t batch, int top_k, int experts, int budget, int variant,
+                               const float* norms, const float* coeff, const float* loss,
+                               int world, int rank, void* const* peers, uint64_t wait_ns,
+                               void* out_w, void* out_ids, int32_t* out_subset, int32_t* status,
+                               exf_stream_t stream) {
+  const char* name = "exf_decode_sharded";
+  int rc = decode_checks(name, w_dtype, id_dtype, batch, top_k, experts, budget, variant);
+  if (rc != EXF_OK) return rc;
+  EXF_REQUIRE(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world,
+              "%s: world must be in [1, %d] and 0 <= rank < world", name, kMaxPeers);
+  EXF_REQUIRE(norms && coeff && loss && peers, "%s: null pointer", name);
+  EXF_REQUIRE(batch == 0 || (w && ids && out_w && out_ids), "%s: null routing pointer", name);
+  DecodeParams p{w, ids, batch * top_k, experts, budget, variant, kImportanceExchanged, norms,
+                 nullptr, nullptr, coeff, loss, out_w, out_ids, out_subset};
+  p.world = world;
+  p.rank = rank;
+  for (int r = 0; r < world; ++r) {
+    EXF_REQUIRE(peers[r] && (reinterpret_cast<uintptr_t>(peers[r]) & 63u) == 0,
+                "%s: exchange buffer of rank %d is null or not 64-byte aligned", name, r);
+    p.peers[r] = static_cast<int64_t*>(peers[r]);
+  }
+  p.status = status;
+  p.wait_ns = wait_ns;
   return cuda_status(launch_decode(w_dtype, id_dtype, p, (cudaStream_t)stream), name);
 }
 

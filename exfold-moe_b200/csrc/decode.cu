@@ -13,6 +13,10 @@
 //   4. apply the table to every route.
 // A decode batch is at most a few thousand routes (B x k), so the single CTA keeps every phase
 // on chip and the transform costs one launch.
+// For a batch sharded over GPUs (kImportanceExchanged) phase 1 is followed by an exchange with the
+// peer ranks inside the launch: each rank's vector goes to every rank's exchange buffer by NVLink
+// peer stores, and every rank sums the R vectors in rank order (exact integers), so one launch per
+// layer replaces importance launch + all-reduce + apply launch.
 // decode_importance_kernel is the multi-CTA first phase for a sharded or very large batch.
 #include <float.h>
 
@@ -66,6 +70,78 @@ __device__ __forceinline__ void argmin_merge(float& v, int& pos, float ov, int o
 template <typename WT, typename IT, bool ALIGN>
 __device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm);
 
+// ---- peer exchange (system-scope release / acquire on the flags) ----------------------------
+__device__ __forceinline__ void st_release_sys(long long* ptr, long long v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ long long ld_acquire_sys(const long long* ptr) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ long long ld_relaxed_sys(const long long* ptr) {
+  long long v;
+  asm volatile("ld.relaxed.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s
+
+// sm.imp holds this rank's vector; afterwards the sum over the ranks (see kXchSlots).  A vector
+// that has not arrived within p.wait_ns (2 s by default) leaves the local vector in place and sets
+// *p.status = 1: the ranks' subsets then differ, and the exchange buffers must be rebuilt.
+__device__ void exchange_importance(const DecodeParams& p, DecodeSmem& sm) {
+  __shared__ long long s_call;
+  __shared__ int s_late;
+  const int E = p.experts, R = p.world, me = p.rank, tid = threadIdx.x;
+  long long* own = reinterpret_cast<long long*>(p.peers[me]);
+  if (tid == 0) {
+    s_call = own[kXchEpoch] + 1;  // written by this rank's previous call (stream order)
+    s_late = 0;
+  }
+  __syncthreads();
+  const long long call = s_call;
+  const int64_t par = call & 1;
+  for (int i = tid; i < R * E; i += kDecodeThreads) {
+    const int r = i / E, e = i - r * E;
+    reinterpret_cast<long long*>(p.peers[r])[kXchSlots + (par * R + me) * E + e] = sm.imp[e];
+  }
+  // the barrier orders every thread's stores before the flag releases (release is cumulative)
+  __syncthreads();
+  if (tid < R) st_release_sys(reinterpret_cast<long long*>(p.peers[tid]) + kXchFlags + 8 * me, call);
+  if (tid < R) {
+    const long long* flag = own + kXchFlags + 8 * tid;
+    const unsigned long long limit = p.wait_ns ? p.wait_ns : kDefaultWaitNs;
+    const unsigned long long t0 = global_ns();
+    // time-bounded, and iteration-bounded too (at least ~4 s of 64 ns sleeps)
+    for (uint32_t it = 0; ld_acquire_sys(flag) < call; ++it) {
+      if (global_ns() - t0 > limit || it >= (1u << 26)) {
+        atomicExch(&s_late, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  if (s_late == 0) {
+    for (int e = tid; e < E; e += kDecodeThreads) {
+      unsigned long long acc = 0;  // modulo 2^64, as the single-GPU sums
+      for (int r = 0; r < R; ++r)
+        acc += (unsigned long long)ld_relaxed_sys(own + kXchSlots + (par * R + r) * E + e);
+      sm.imp[e] = (long long)acc;
+    }
+  }
+  if (tid == 0) {
+    own[kXchEpoch] = call;
+    if (s_late != 0 && p.status) *p.status = 1;
+  }
+  __syncthreads();
+}
+
 template <typename WT, typename IT, bool ALIGN = false>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeParams p) {
   __shared__ DecodeSmem sm;
@@ -81,15 +157,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   // ---- 1. importance ------------------------------------------------------------------------
   const int copies = kHistLongs / E < 32 ? kHistLongs / E : 32;  // >= 2 for E <= 1024
   long long* hist = sm.hist + ((tid >> 5) % copies) * E;
+  const bool from_routes = p.source == kImportanceFromRoutes || p.source == kImportanceExchanged;
   for (int e = tid; e < E; e += kDecodeThreads) {
     sm.imp[e] = (p.source == kImportanceGiven) ? p.importance[e] : 0;
-    if (p.source == kImportanceFromRoutes) sm.norm[e] = __ldg(p.norms + e);
+    if (from_routes) sm.norm[e] = __ldg(p.norms + e);
     sm.keep[e] = 0;
   }
-  if (p.source == kImportanceFromRoutes)
+  if (from_routes)
     for (int i = tid; i < copies * E; i += kDecodeThreads) sm.hist[i] = 0;
   __syncthreads();
-  if (p.source == kImportanceFromRoutes) {
+  if (from_routes) {
     for (int64_t base = 0; base < p.routes; base += kRouteUnroll * kDecodeThreads) {
       WT wr[kRouteUnroll];
       int er[kRouteUnroll];
@@ -115,6 +192,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
     }
     __syncthreads();
   }
+  if (p.source == kImportanceExchanged) exchange_importance(p, sm);
 
   // ---- 2. order -------------------------------------------------------------------------------
   if (p.source == kSubsetGiven) {

@@ -40,7 +40,30 @@ struct FoldParams {
   void* out_ids;
 };
 
-enum DecodeSource { kImportanceFromRoutes = 0, kImportanceGiven = 1, kSubsetGiven = 2 };
+enum DecodeSource {
+  kImportanceFromRoutes = 0,
+  kImportanceGiven = 1,
+  kSubsetGiven = 2,
+  kImportanceExchanged = 3  // from routes, then summed with the peer ranks' vectors in-launch
+};
+
+// Peer exchange of the sharded decode importance.  Every rank owns one buffer of
+// exchange_longs(E, R) int64 (zeroed before first use) laid out as
+//   [kXchEpoch]                 calls made so far on this buffer (written by its own rank only)
+//   [kXchFlags + 8 r]           the last call number whose vector rank r has delivered here
+//   [kXchSlots + (p R + r) E]   rank r's importance vector of a call with parity p
+// A call numbered c writes this rank's vector into slot (c & 1, rank) of every rank's buffer by
+// NVLink peer stores, publishes c in every rank's flag `rank` (release, system scope), waits
+// (bounded) until its own R flags reach c, and sums the R vectors of parity c & 1 in rank order.
+// Two parities suffice: a rank writes call c + 2 only after every rank has published call c + 1,
+// which each does only after finishing call c.
+constexpr int kMaxPeers = 8;
+constexpr int64_t kXchEpoch = 0;
+constexpr int64_t kXchFlags = 16;
+constexpr int64_t kXchSlots = 16 + 8 * kMaxPeers;
+constexpr int64_t exchange_longs(int experts, int world) {
+  return kXchSlots + 2 * static_cast<int64_t>(world) * experts;
+}
 
 struct DecodeParams {
   const void* w;
@@ -66,6 +89,12 @@ struct DecodeParams {
   int32_t* sorted_ids;      // moe_align outputs over gemm_ids, 128-row blocks
   int32_t* block_experts;
   int32_t* num_post_pad;
+  // kImportanceExchanged only: this process's mapping of every rank's exchange buffer
+  int world;
+  int rank;
+  int64_t* peers[kMaxPeers];
+  int32_t* status;          // set to 1 when a peer's vector did not arrive in time (may be null)
+  unsigned long long wait_ns;
 };
 
 struct AlignParams {

@@ -41,6 +41,12 @@ SIGNATURES = {
     "exf_decode_importance": (_i, [_vp, _i, _vp, _i, _i64, _i, _vp, _vp, _vp]),
     "exf_decode_apply": (_i, [_vp, _vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
                               _vp]),
+    "exf_decode_exchange_bytes": (_i64, [_i, _i]),
+    "exf_decode_sharded": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp,
+                                ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp]),
+    "exf_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(_i64)]),
+    "exf_ipc_import": (_i, [_vp, _i64, ctypes.POINTER(_vp)]),
+    "exf_ipc_release": (_i, [_vp, _i64]),
     "exf_reroute_subset": (_i, [_vp, _i, _vp, _i, _i64, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
     "exf_static_table": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     "exf_static_remap": (_i, [_vp, _i, _vp, _i, _i64, _i, _vp, _vp, _vp]),

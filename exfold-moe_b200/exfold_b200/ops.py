@@ -202,6 +202,27 @@ def decode_apply(importance: torch.Tensor, weights: torch.Tensor, ids: torch.Ten
     return ow.to(weights.dtype), oi.to(ids.dtype)
 
 
+def decode_sharded(weights: torch.Tensor, ids: torch.Tensor, norms: torch.Tensor,
+                   coeff: torch.Tensor, loss: torch.Tensor, budget: int, *, world: int, rank: int,
+                   peers: "ctypes.Array", variant: str = "qwen3",
+                   status: torch.Tensor | None = None, wait_ns: int = 0,
+                   subset_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Decode budget of this rank's shard in one launch, the importance exchanged with the other
+    ranks over peer memory (`peers`: every rank's exchange buffer as mapped here, a ctypes array
+    of `world` device pointers; see `exfold_b200.parallel.DecodeExchange`)."""
+    dev = _require_cuda(weights, ids, norms, coeff, loss, status)
+    w_in, i_in = _weights_in(weights), _ids_in(ids)
+    batch, top_k = w_in.shape
+    norms, coeff, loss = _f32c(norms), _f32c(coeff), _f32c(loss)
+    ow, oi = torch.empty_like(w_in), torch.empty_like(i_in)
+    L.check(L.lib().exf_decode_sharded(
+        w_in.data_ptr(), _WDT[w_in.dtype], i_in.data_ptr(), _IDT[i_in.dtype], batch, top_k,
+        coeff.shape[0], int(budget), _VARIANT[variant], norms.data_ptr(), coeff.data_ptr(),
+        loss.data_ptr(), int(world), int(rank), peers, int(wait_ns), ow.data_ptr(), oi.data_ptr(),
+        _ptr(subset_out), _ptr(status), _stream(dev)))
+    return ow.to(weights.dtype), oi.to(ids.dtype)
+
+
 def reroute_subset(weights: torch.Tensor, ids: torch.Tensor, subset: torch.Tensor,
                    coeff: torch.Tensor, loss: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     dev = _require_cuda(weights, ids, subset, coeff, loss)

@@ -4,20 +4,87 @@ Prefill: every rank routes and folds its own contiguous token shard; there is no
 the ids are identical to a single-GPU run.
 
 Decode: the expert budget needs the importance of the whole batch.  Each rank adds its routes'
-importance, as exact 2^-32 fixed point, into an int64 [E] vector; one all-reduce (sum) gives
-every rank the batch's vector; each rank then selects the same top-D subset and applies the
-table to its own routes.  Integer sums are exact and order independent, so the result equals the
-single-GPU decode bit for bit at any world size.
+importance, as exact 2^-32 fixed point, into an int64 [E] vector; the ranks sum the vectors;
+each rank then selects the same top-D subset and applies the table to its own routes.  Integer
+sums are exact and order independent, so the result equals the single-GPU decode bit for bit at
+any world size.  Two ways to sum:
+
+* `DecodeExchange` (one launch per layer): every rank maps every other rank's exchange buffer
+  (CUDA IPC), and the decode launch itself writes its vector into all of them over NVLink,
+  waits for theirs and sums (`ops.decode_sharded`);
+* `sharded_decode` (three steps): importance launch, an all-reduce of E int64 through the
+  process group, apply launch.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import ops
+
+
+class DecodeExchange:
+    """Exchange buffers of the sharded decode for the ranks of one process group, one process
+    per GPU of a node (at most 8 ranks).
+
+    Every rank allocates a zeroed buffer of exf_decode_exchange_bytes(E, R) bytes, exports it
+    with CUDA IPC, the handles are all-gathered through the group, each rank maps the others'
+    buffers, and a barrier makes sure that every buffer is zeroed before any rank's first call
+    writes into it.  `decode` is then one launch per layer; every rank must make the same
+    sequence of calls (like a collective).  A device int32 `status` is set to 1 when a rank's
+    vector did not arrive within `wait_ns` (2 s by default); the exchange must then be rebuilt.
+    """
+
+    def __init__(self, experts: int, *, group: dist.ProcessGroup | None = None,
+                 device: torch.device | None = None):
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.experts = int(experts)
+        nbytes = int(L.lib().exf_decode_exchange_bytes(self.experts, self.world))
+        if nbytes <= 0:
+            raise ValueError(f"no exchange for {experts} experts over {self.world} ranks "
+                             "(at most 1024 experts and 8 ranks)")
+        self.buffer = torch.zeros(nbytes // 8, dtype=torch.int64, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.buffer.device)
+        self._imported: list[tuple[int, int]] = []
+        ptrs = (ctypes.c_void_p * self.world)()
+        if self.world == 1:
+            ptrs[0] = self.buffer.data_ptr()
+        else:
+            handle = (ctypes.c_char * 64)()
+            offset = ctypes.c_int64()
+            L.check(L.lib().exf_ipc_export(self.buffer.data_ptr(), handle, ctypes.byref(offset)))
+            entries: list = [None] * self.world
+            dist.all_gather_object(entries, (bytes(handle), offset.value), group=group)
+            for r, (h, off) in enumerate(entries):
+                if r == self.rank:
+                    ptrs[r] = self.buffer.data_ptr()
+                    continue
+                mapped = ctypes.c_void_p()
+                L.check(L.lib().exf_ipc_import(h, off, ctypes.byref(mapped)))
+                ptrs[r] = mapped.value
+                self._imported.append((mapped.value, off))
+            torch.cuda.synchronize(self.buffer.device)
+            dist.barrier(group=group)
+        self.peers = ptrs
+
+    def decode(self, weights: torch.Tensor, ids: torch.Tensor, norms: torch.Tensor,
+               coeff: torch.Tensor, loss: torch.Tensor, budget: int, *, variant: str = "qwen3",
+               wait_ns: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+        return ops.decode_sharded(weights, ids, norms, coeff, loss, budget, world=self.world,
+                                  rank=self.rank, peers=self.peers, variant=variant,
+                                  status=self.status, wait_ns=wait_ns)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (after every call using them has finished)."""
+        for ptr, off in self._imported:
+            L.check(L.lib().exf_ipc_release(ctypes.c_void_p(ptr), off))
+        self._imported = []
 
 
 def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:

@@ -133,6 +133,38 @@ EXF_API int exf_decode_apply(const int64_t* importance, const void* w, int w_dty
                              const float* loss, void* out_w, void* out_ids, int32_t* out_subset,
                              exf_stream_t stream);
 
+/* Sharded decode in one launch per layer, the importance exchanged over NVLink peer memory
+ * instead of an all-reduce between two launches.  Each of `world` <= 8 ranks (one process per
+ * GPU) holds its shard [batch][top_k] of the decode batch and one exchange buffer of
+ * exf_decode_exchange_bytes(experts, world) bytes, zeroed before first use and 64-byte aligned;
+ * `peers` (host array of `world` device pointers) gives every rank's buffer as mapped in this
+ * process (peers[rank] = its own; the others from exf_ipc_import).  The launch adds this shard's
+ * fixed-point importance, writes it into every rank's buffer, publishes it with a system-scope
+ * release flag, waits until every rank's vector has arrived, and sums them in rank order, then
+ * selects, builds the table and applies it to its own routes: results equal exf_decode on the
+ * unsharded batch bit for bit.  Like a collective, every rank must make the same sequence of
+ * calls on its buffer (same experts, world, budget and variant), each on one stream.
+ * A wait is bounded by wait_ns (0: 2 s); when it runs out, *status (device int32, may be NULL)
+ * is set to 1, the result uses this rank's importance only, and the buffers must be rebuilt.
+ * Replaces exf_decode_importance + an all-reduce + exf_decode_apply. */
+EXF_API int64_t exf_decode_exchange_bytes(int experts, int world);
+EXF_API int exf_decode_sharded(const void* w, int w_dtype, const void* ids, int id_dtype,
+                               int64_t batch, int top_k, int experts, int budget, int variant,
+                               const float* norms, const float* coeff, const float* loss,
+                               int world, int rank, void* const* peers, uint64_t wait_ns,
+                               void* out_w, void* out_ids, int32_t* out_subset, int32_t* status,
+                               exf_stream_t stream);
+
+/* CUDA IPC of a device buffer between the processes of one node (cudaIpcGetMemHandle /
+ * cudaIpcOpenMemHandle with lazy peer access): export gives a 64-byte handle of the cudaMalloc
+ * allocation holding `ptr` and ptr's offset in it; import maps another process's allocation and
+ * returns the mapped address plus that offset; release unmaps an imported address.  The buffer
+ * must come from cudaMalloc (or an allocator built on it), not from virtual-memory mappings. */
+#define EXF_IPC_HANDLE_BYTES 64
+EXF_API int exf_ipc_export(const void* ptr, void* handle, int64_t* offset);
+EXF_API int exf_ipc_import(const void* handle, int64_t offset, void** ptr);
+EXF_API int exf_ipc_release(void* ptr, int64_t offset);
+
 /* Reroute to an explicit subset (importance order given by the caller): replaces
  * reroute_decode_subset / _reroute_decode_kernel (exfold/qwen3/kernels.py:235-292, 154-232).
  * subset [subset_size] int32 expert ids. */

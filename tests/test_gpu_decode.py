@@ -232,3 +232,66 @@ def test_decode_nan_and_huge_products(variant):
                               variant=variant)
     np.testing.assert_array_equal(host(si), ei)
     np.testing.assert_array_equal(host(sw), ew)
+
+
+def test_sharded_exchange_single_rank_equals_decode():
+    """The one-launch sharded decode with one rank (its own buffer as the only peer) equals the
+    plain decode, over consecutive calls (the call counter advances) and in a replayed graph."""
+    from exfold_b200.parallel import DecodeExchange
+
+    xch = DecodeExchange(128, device=DEV)
+    layers = [W.layer("qwen3_decode", layer_index=i) for i in range(3)]
+    cases = []
+    for lay in layers:
+        rw, ri = O.router_topk(lay.logits, 8, "softmax")
+        cases.append(tuple(cuda(a) for a in (rw, ri, lay.norms, lay.coeff, lay.loss)))
+    for variant in ("qwen3", "dsv4"):
+        for w, i, n, c, l_ in cases:
+            gw, gi = xch.decode(w, i, n, c, l_, 64, variant=variant)
+            ew, ei = ops.decode(w, i, n, c, l_, 64, variant=variant)
+            assert torch.equal(gi, ei) and torch.equal(gw, ew)
+    s = torch.cuda.Stream(DEV)
+    outs = []
+    with torch.cuda.stream(s):
+        xch.decode(*cases[0], 64)
+        torch.cuda.synchronize(DEV)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for case in cases:
+                outs.append(xch.decode(*case, 64))
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize(DEV)
+    for (gw, gi), case in zip(outs, cases):
+        ew, ei = ops.decode(*case, 64)
+        assert torch.equal(gi, ei) and torch.equal(gw, ew)
+    assert int(xch.status.item()) == 0
+    assert int(xch.buffer[0].item()) == 6 + 1 + 3 * 3  # calls made on the buffer
+
+
+def test_sharded_exchange_missing_rank_times_out_with_status():
+    """Failure detection without a fault: rank 0 of two, the second rank's buffer a local one that
+    no kernel ever publishes to.  The bounded wait (2 ms here) runs out, the status is set, and the
+    result is the decode with this rank's importance alone; the context stays usable."""
+    import ctypes
+
+    from exfold_b200 import _lib as L
+
+    nbytes = int(L.lib().exf_decode_exchange_bytes(128, 2))
+    bufs = [torch.zeros(nbytes // 8, dtype=torch.int64, device=DEV) for _ in range(2)]
+    peers = (ctypes.c_void_p * 2)(bufs[0].data_ptr(), bufs[1].data_ptr())
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lay = W.layer("qwen3_decode")
+    rw, ri = O.router_topk(lay.logits, 8, "softmax")
+    w, i, n, c, l_ = (cuda(a) for a in (rw, ri, lay.norms, lay.coeff, lay.loss))
+    for call in (1, 2):
+        gw, gi = ops.decode_sharded(w, i, n, c, l_, 64, world=2, rank=0, peers=peers,
+                                    status=status, wait_ns=2_000_000)
+        ew, ei = ops.decode(w, i, n, c, l_, 64)
+        torch.cuda.synchronize(DEV)
+        assert int(status.item()) == 1
+        assert torch.equal(gi, ei) and torch.equal(gw, ew)
+        assert int(bufs[0][0].item()) == call
+        assert int(bufs[1][16].item()) == call  # the flag this rank published to its peer
+    # the context is intact
+    assert torch.equal(ops.decode(w, i, n, c, l_, 64)[1], ei)
