@@ -318,7 +318,12 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
         w[layer].copy_(lw)
         ids[layer].copy_(li)
     imp = torch.zeros((LAYERS, EXPERTS), dtype=torch.int64, device=dev)
-    xch = parallel.DecodeExchange(EXPERTS, device=dev) if world > 1 else None
+    xch, xch_error = None, None
+    if world > 1:
+        try:
+            xch = parallel.DecodeExchange(EXPERTS, device=dev)
+        except RuntimeError as exc:  # every rank sees the same outcome
+            xch_error = str(exc)
 
     def step(outs: list, how: str):
         for layer in range(LAYERS):
@@ -345,22 +350,28 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
         return graph, results
 
     steps = max(10, args.steps // 10)
-    graph, results = capture("exchange")
+    main = "all_reduce" if xch_error else "exchange"
+    graph, results = capture(main)
     ms = timed(graph.replay, steps) / steps
     out = {"workload": "qwen3_layers_decode", "batch": DECODE_BATCH,
            "batch_per_gpu": end - start, "budget": DECODE_BUDGET, "layers": LAYERS,
            "us_per_layer": 1e3 * ms / LAYERS, "scaling": "strong (B fixed)",
-           "launches_per_layer": 1,
-           "collective": None if world == 1 else
-           "in-launch exchange of int64[128] over NVLink peer memory (CUDA IPC)"}
+           "launches_per_layer": 2 if xch_error else 1,
+           "collective": None if world == 1 else (
+               "NCCL all_reduce int64[128] per layer" if xch_error else
+               "in-launch exchange of int64[128] over NVLink peer memory (CUDA IPC)")}
+    if xch_error:
+        out["exchange_unavailable"] = xch_error
     if world > 1:
-        runs = {"exchange": (graph, results)}
-        graph_nccl, results_nccl = capture("all_reduce")
-        ms_nccl = timed(graph_nccl.replay, steps) / steps
-        runs["all_reduce"] = (graph_nccl, results_nccl)
-        out["all_reduce_path"] = {"us_per_layer": 1e3 * ms_nccl / LAYERS,
-                                  "launches_per_layer": 2,
-                                  "collective": "NCCL all_reduce int64[128] per layer"}
+        runs = {main: (graph, results)}
+        graph_nccl, results_nccl = None, None
+        if not xch_error:
+            graph_nccl, results_nccl = capture("all_reduce")
+            ms_nccl = timed(graph_nccl.replay, steps) / steps
+            runs["all_reduce"] = (graph_nccl, results_nccl)
+            out["all_reduce_path"] = {"us_per_layer": 1e3 * ms_nccl / LAYERS,
+                                      "launches_per_layer": 2,
+                                      "collective": "NCCL all_reduce int64[128] per layer"}
         same = True
         with torch.cuda.stream(stream):
             refs = []
@@ -373,14 +384,15 @@ def measure_decode(dev, world, rank, stream, coeff, loss, timed, args) -> dict:
                 g.replay()
                 for (gw, gi), (ew, ei) in zip(res, refs):
                     same = same and bool(torch.equal(ei, gi)) and bool(torch.equal(ew, gw))
-        same = same and int(xch.status.item()) == 0
+        same = same and (xch is None or int(xch.status.item()) == 0)
         flag = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         out["decode_parity"] = bool(flag.item())
         del runs, graph_nccl, results_nccl
         torch.cuda.synchronize(dev)
         dist.barrier()
-        xch.close()
+        if xch is not None:
+            xch.close()
     del graph, results
     return out
 

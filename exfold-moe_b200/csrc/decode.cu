@@ -70,18 +70,13 @@ __device__ __forceinline__ void argmin_merge(float& v, int& pos, float ov, int o
 template <typename WT, typename IT, bool ALIGN>
 __device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm);
 
-// ---- peer exchange (system-scope release / acquire on the flags) ----------------------------
-__device__ __forceinline__ void st_release_sys(long long* ptr, long long v) {
-  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+// ---- peer exchange: self-validating 8-byte words (see kXchSlots) ------------------------------
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
-__device__ __forceinline__ long long ld_acquire_sys(const long long* ptr) {
-  long long v;
-  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
-  return v;
-}
-__device__ __forceinline__ long long ld_relaxed_sys(const long long* ptr) {
-  long long v;
-  asm volatile("ld.relaxed.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* ptr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
   return v;
 }
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -91,50 +86,61 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s
 
-// sm.imp holds this rank's vector; afterwards the sum over the ranks (see kXchSlots).  A vector
-// that has not arrived within p.wait_ns (2 s by default) leaves the local vector in place and sets
+// sm.imp holds this rank's vector; afterwards the sum over the ranks.  A word that has not
+// arrived within p.wait_ns (2 s by default) leaves the local vector in place and sets
 // *p.status = 1: the ranks' subsets then differ, and the exchange buffers must be rebuilt.
 __device__ void exchange_importance(const DecodeParams& p, DecodeSmem& sm) {
-  __shared__ long long s_call;
+  __shared__ unsigned long long s_call;
   __shared__ int s_late;
   const int E = p.experts, R = p.world, me = p.rank, tid = threadIdx.x;
-  long long* own = reinterpret_cast<long long*>(p.peers[me]);
+  unsigned long long* own = reinterpret_cast<unsigned long long*>(p.peers[me]);
   if (tid == 0) {
     s_call = own[kXchEpoch] + 1;  // written by this rank's previous call (stream order)
     s_late = 0;
   }
   __syncthreads();
-  const long long call = s_call;
-  const int64_t par = call & 1;
-  for (int i = tid; i < R * E; i += kDecodeThreads) {
-    const int r = i / E, e = i - r * E;
-    reinterpret_cast<long long*>(p.peers[r])[kXchSlots + (par * R + me) * E + e] = sm.imp[e];
+  const unsigned long long call = s_call;
+  const unsigned long long tag = (call & 0xFFFFFFFFull) << 32;
+  const int64_t par = static_cast<int64_t>(call & 1);
+  // this rank's words into slot (par, me) of every rank's buffer
+  for (int i = tid; i < R * E * 2; i += kDecodeThreads) {
+    const int r = i / (2 * E), k = i - r * 2 * E;  // k = 2 e + h
+    const unsigned long long v = static_cast<unsigned long long>(sm.imp[k >> 1]);
+    const unsigned long long half = (k & 1) ? (v >> 32) : (v & 0xFFFFFFFFull);
+    st_relaxed_sys(reinterpret_cast<unsigned long long*>(p.peers[r]) + kXchSlots +
+                       ((par * R + me) * E) * 2 + k,
+                   tag | half);
   }
-  // the barrier orders every thread's stores before the flag releases (release is cumulative)
-  __syncthreads();
-  if (tid < R) st_release_sys(reinterpret_cast<long long*>(p.peers[tid]) + kXchFlags + 8 * me, call);
-  if (tid < R) {
-    const long long* flag = own + kXchFlags + 8 * tid;
-    const unsigned long long limit = p.wait_ns ? p.wait_ns : kDefaultWaitNs;
-    const unsigned long long t0 = global_ns();
-    // time-bounded, and iteration-bounded too (at least ~4 s of 64 ns sleeps)
-    for (uint32_t it = 0; ld_acquire_sys(flag) < call; ++it) {
-      if (global_ns() - t0 > limit || it >= (1u << 26)) {
-        atomicExch(&s_late, 1);
-        break;
+  __syncthreads();  // every local read of sm.imp is done before it is overwritten below
+  // poll this rank's slots of parity par; each thread owns whole experts (both halves, all r)
+  const unsigned long long limit = p.wait_ns ? p.wait_ns : kDefaultWaitNs;
+  const unsigned long long t0 = global_ns();
+  bool late = false;
+  for (int e = tid; e < E; e += kDecodeThreads) {
+    unsigned long long acc = 0;  // modulo 2^64, as the single-GPU sums
+    for (int r = 0; r < R; ++r) {
+      const unsigned long long* wp = own + kXchSlots + ((par * R + r) * E + e) * 2;
+      unsigned long long lo = ld_relaxed_sys(wp), hi = ld_relaxed_sys(wp + 1);
+      // time-bounded, and iteration-bounded too (at least ~4 s of 64 ns sleeps)
+      for (uint32_t it = 0; !late && ((lo ^ tag) >> 32 || (hi ^ tag) >> 32); ++it) {
+        if (global_ns() - t0 > limit || it >= (1u << 26)) {
+          late = true;
+          break;
+        }
+        __nanosleep(64);
+        lo = ld_relaxed_sys(wp);
+        hi = ld_relaxed_sys(wp + 1);
       }
-      __nanosleep(64);
+      acc += (hi << 32) | (lo & 0xFFFFFFFFull);
     }
+    // staged in hist (free between phases 1 and 2) so that sm.imp changes only if every
+    // rank's vector arrived
+    if (!late) sm.hist[e] = static_cast<long long>(acc);
   }
+  if (late) atomicExch(&s_late, 1);
   __syncthreads();
-  if (s_late == 0) {
-    for (int e = tid; e < E; e += kDecodeThreads) {
-      unsigned long long acc = 0;  // modulo 2^64, as the single-GPU sums
-      for (int r = 0; r < R; ++r)
-        acc += (unsigned long long)ld_relaxed_sys(own + kXchSlots + (par * R + r) * E + e);
-      sm.imp[e] = (long long)acc;
-    }
-  }
+  if (s_late == 0)
+    for (int e = tid; e < E; e += kDecodeThreads) sm.imp[e] = sm.hist[e];
   if (tid == 0) {
     own[kXchEpoch] = call;
     if (s_late != 0 && p.status) *p.status = 1;

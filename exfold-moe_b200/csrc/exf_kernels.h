@@ -48,21 +48,22 @@ enum DecodeSource {
 };
 
 // Peer exchange of the sharded decode importance.  Every rank owns one buffer of
-// exchange_longs(E, R) int64 (zeroed before first use) laid out as
-//   [kXchEpoch]                 calls made so far on this buffer (written by its own rank only)
-//   [kXchFlags + 8 r]           the last call number whose vector rank r has delivered here
-//   [kXchSlots + (p R + r) E]   rank r's importance vector of a call with parity p
-// A call numbered c writes this rank's vector into slot (c & 1, rank) of every rank's buffer by
-// NVLink peer stores, publishes c in every rank's flag `rank` (release, system scope), waits
-// (bounded) until its own R flags reach c, and sums the R vectors of parity c & 1 in rank order.
-// Two parities suffice: a rank writes call c + 2 only after every rank has published call c + 1,
-// which each does only after finishing call c.
+// exchange_longs(E, R) 64-bit words (zeroed before first use) laid out as
+//   [kXchEpoch]                      calls made so far on this buffer (written by its rank only)
+//   [kXchSlots + ((p R + r) E + e) 2 + h]   half h of rank r's importance of expert e, written
+//                                            by rank r during a call of parity p
+// Each word is (call number << 32) | 32-bit half, stored with one 8-byte store (single-copy
+// atomic), so a receiver that reads the current call number in a word also reads its half: no
+// fence or separate flag is needed.  A call numbered c writes this rank's vector into slot
+// (c & 1, rank) of every rank's buffer by NVLink peer stores, then polls (bounded) its own slots
+// of parity c & 1 until every word carries c, and sums the R vectors in rank order.  Two
+// parities suffice: a rank writes call c + 2 only after reading every rank's call c + 1, which
+// each rank writes only after finishing call c.
 constexpr int kMaxPeers = 8;
 constexpr int64_t kXchEpoch = 0;
-constexpr int64_t kXchFlags = 16;
-constexpr int64_t kXchSlots = 16 + 8 * kMaxPeers;
+constexpr int64_t kXchSlots = 16;
 constexpr int64_t exchange_longs(int experts, int world) {
-  return kXchSlots + 2 * static_cast<int64_t>(world) * experts;
+  return kXchSlots + 4 * static_cast<int64_t>(world) * experts;
 }
 
 struct DecodeParams {

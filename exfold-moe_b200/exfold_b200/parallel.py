@@ -56,21 +56,35 @@ class DecodeExchange:
         if self.world == 1:
             ptrs[0] = self.buffer.data_ptr()
         else:
+            # every rank takes the same collective steps whether its own export / imports
+            # succeed or not, and all of them raise together if any rank failed
+            lib = L.lib()
             handle = (ctypes.c_char * 64)()
             offset = ctypes.c_int64()
-            L.check(L.lib().exf_ipc_export(self.buffer.data_ptr(), handle, ctypes.byref(offset)))
+            rc = lib.exf_ipc_export(self.buffer.data_ptr(), handle, ctypes.byref(offset))
+            mine = (bytes(handle), offset.value) if rc == L.EXF_OK else None
+            error = None if rc == L.EXF_OK else lib.exf_last_error().decode(errors="replace")
             entries: list = [None] * self.world
-            dist.all_gather_object(entries, (bytes(handle), offset.value), group=group)
-            for r, (h, off) in enumerate(entries):
-                if r == self.rank:
-                    ptrs[r] = self.buffer.data_ptr()
-                    continue
-                mapped = ctypes.c_void_p()
-                L.check(L.lib().exf_ipc_import(h, off, ctypes.byref(mapped)))
-                ptrs[r] = mapped.value
-                self._imported.append((mapped.value, off))
+            dist.all_gather_object(entries, mine, group=group)
+            if all(e is not None for e in entries):
+                for r, (h, off) in enumerate(entries):
+                    if r == self.rank:
+                        ptrs[r] = self.buffer.data_ptr()
+                        continue
+                    mapped = ctypes.c_void_p()
+                    if lib.exf_ipc_import(h, off, ctypes.byref(mapped)) != L.EXF_OK:
+                        error = lib.exf_last_error().decode(errors="replace")
+                        break
+                    ptrs[r] = mapped.value
+                    self._imported.append((mapped.value, off))
+            else:
+                error = error or "another rank could not export its exchange buffer"
             torch.cuda.synchronize(self.buffer.device)
-            dist.barrier(group=group)
+            ok = torch.tensor([0 if error else 1], dtype=torch.int32, device=self.buffer.device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok.item()) == 0:
+                self.close()
+                raise RuntimeError(f"decode exchange setup failed: {error or 'on another rank'}")
         self.peers = ptrs
 
     def decode(self, weights: torch.Tensor, ids: torch.Tensor, norms: torch.Tensor,

@@ -139,10 +139,11 @@ EXF_API int exf_decode_apply(const int64_t* importance, const void* w, int w_dty
  * exf_decode_exchange_bytes(experts, world) bytes, zeroed before first use and 64-byte aligned;
  * `peers` (host array of `world` device pointers) gives every rank's buffer as mapped in this
  * process (peers[rank] = its own; the others from exf_ipc_import).  The launch adds this shard's
- * fixed-point importance, writes it into every rank's buffer, publishes it with a system-scope
- * release flag, waits until every rank's vector has arrived, and sums them in rank order, then
- * selects, builds the table and applies it to its own routes: results equal exf_decode on the
- * unsharded batch bit for bit.  Like a collective, every rank must make the same sequence of
+ * fixed-point importance, writes it into every rank's buffer as 8-byte words that each carry the
+ * call number beside half a value (so a word that shows the current call is complete: no fence
+ * or flag round trip), waits until every rank's words of this call have arrived, and sums the
+ * vectors in rank order, then selects, builds the table and applies it to its own routes:
+ * results equal exf_decode on the unsharded batch bit for bit.  Like a collective, every rank must make the same sequence of
  * calls on its buffer (same experts, world, budget and variant), each on one stream.
  * A wait is bounded by wait_ns (0: 2 s); when it runs out, *status (device int32, may be NULL)
  * is set to 1, the result uses this rank's importance only, and the buffers must be rebuilt.

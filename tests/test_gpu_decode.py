@@ -292,6 +292,8 @@ def test_sharded_exchange_missing_rank_times_out_with_status():
         assert int(status.item()) == 1
         assert torch.equal(gi, ei) and torch.equal(gw, ew)
         assert int(bufs[0][0].item()) == call
-        assert int(bufs[1][16].item()) == call  # the flag this rank published to its peer
+        # the words this rank published to its peer's slot (parity call & 1, rank 0) carry call
+        word = int(bufs[1][16 + (call & 1) * 2 * 128 * 2].item())
+        assert word >> 32 == call
     # the context is intact
     assert torch.equal(ops.decode(w, i, n, c, l_, 64)[1], ei)
