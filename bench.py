@@ -21,6 +21,7 @@ The same line carries the rest of the metric "fold-transform tokens/s & MoE-laye
   I = 2048), config 3 (DeepSeek-style decode sweep, B in {8, 32, 128, 512} x D in {64, 128},
   transform and expert layer).  Inputs that fit in L2 are timed one launch at a time with L2
   flushed (a 512 MiB write) between launches, outside the timed events;
+* `bf16_logits`: the headline step on bf16 logits (read natively, converted exactly);
 * `cpu_baseline`: the CPU oracle on every host core over a bounded sample of the 48 layers.
 
 --impl reference runs the reference's CPU path for the same metric and config: the CPU oracle (a
@@ -802,12 +803,37 @@ def run_ours(args) -> None:
                 ev_back[b].record(copy_out)
             stream.wait_stream(copy_out)
 
+        # the same step on bf16 logits (the gate output dtype of the served models)
+        logits_bf16 = logits.to(torch.bfloat16)
+
+        def step_bf16():
+            for layer in range(LAYERS):
+                ops.router_fold_prefill(logits_bf16[layer], TOP_K, KEEP, coeff[layer],
+                                        loss[layer], out=(out_w[layer], out_ids[layer]))
+
+        with torch.cuda.stream(stream):
+            step_bf16()
+            torch.cuda.synchronize(dev)
+            g16 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g16, stream=stream):
+                step_bf16()
+            ms_16 = timed(g16.replay, args.steps) / args.steps
+        del g16, logits_bf16
+        bytes_16 = TOKENS * (EXPERTS * 2 + KEEP * 8) + 2 * EXPERTS * EXPERTS * 4
+        launch_16 = ms_16 / 1e3 / LAYERS
+        bf16 = {"value": tokens_per_step / (ms_16 / 1e3), "unit": UNIT, "ms_per_step": ms_16,
+                "us_per_launch": launch_16 * 1e6, "bytes_per_launch": bytes_16,
+                "achieved_gbs": bytes_16 / launch_16 / 1e9,
+                "frac": bytes_16 / launch_16 / 1e9 / peaks["hbm_gbs"],
+                "kernel": "exf::router_tpt_kernel<qwen3 fold, P=4, bf16>"}
+
         if args.workload == "prefill_only":  # profiling: the timed prefill step alone
             if rank == 0:
                 print(json.dumps({"workload": "prefill_only", "layers": LAYERS,
                                   "tokens": TOKENS, "us_per_launch": launch_s * 1e6,
                                   "frac": achieved / peaks["hbm_gbs"],
-                                  "batched_us_per_layer": 1e3 * ms_b / LAYERS}), flush=True)
+                                  "batched_us_per_layer": 1e3 * ms_b / LAYERS,
+                                  "bf16": bf16}), flush=True)
             del graph, gb
             if world > 1:
                 dist.destroy_process_group()
@@ -868,6 +894,7 @@ def run_ours(args) -> None:
                          "us_per_launch": launch_s * 1e6},
             "layer_batched": {"ms_per_step": ms_b, "value": tokens_per_step / (ms_b / 1e3),
                               "launches_per_step": 1},
+            "bf16_logits": bf16,
             "e2e": {"value": tokens_per_step / (ms_e2e / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e, "steps": e2e_steps},

@@ -82,13 +82,14 @@ static bool good_idtype(int d) { return d == EXF_I32 || d == EXF_I64; }
 // ---- entry points ---------------------------------------------------------------------------
 extern "C" {
 
-EXF_API int exf_abi_version(void) { return 1; }
+EXF_API int exf_abi_version(void) { return 2; }
 
 EXF_API const char* exf_last_error(void) { return g_err; }
 
-static int router_common(const char* name, const float* logits, int64_t tokens, int layers,
-                         int experts, int top_k, int scoring, const float* out_w,
+static int router_common(const char* name, const void* logits, int logit_dtype, int64_t tokens,
+                         int layers, int experts, int top_k, int scoring, const float* out_w,
                          const int32_t* out_ids) {
+  EXF_REQUIRE(good_wdtype(logit_dtype), "%s: logits must be EXF_F32, EXF_BF16 or EXF_F16", name);
   EXF_REQUIRE(tokens >= 0 && layers >= 1, "%s: tokens must be >= 0 and layers >= 1", name);
   EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
   EXF_REQUIRE(experts >= top_k, "%s: experts (%d) < top_k (%d)", name, experts, top_k);
@@ -104,21 +105,21 @@ static int router_common(const char* name, const float* logits, int64_t tokens, 
   return EXF_OK;
 }
 
-EXF_API int exf_router_topk(const float* logits, int64_t tokens, int experts, int top_k,
-                            int scoring, const float* bias, int renormalize, float scaling,
-                            float* out_w, int32_t* out_ids, exf_stream_t stream) {
-  int rc = router_common("exf_router_topk", logits, tokens, 1, experts, top_k, scoring, out_w,
-                         out_ids);
+EXF_API int exf_router_topk(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                            int top_k, int scoring, const float* bias, int renormalize,
+                            float scaling, float* out_w, int32_t* out_ids, exf_stream_t stream) {
+  int rc = router_common("exf_router_topk", logits, logit_dtype, tokens, 1, experts, top_k,
+                         scoring, out_w, out_ids);
   if (rc != EXF_OK) return rc;
   if (tokens == 0) return EXF_OK;
   EXF_REQUIRE(!bias || aligned16(bias), "exf_router_topk: bias must be 16-byte aligned");
   RouterParams p{logits, tokens, 1, top_k, bias, renormalize, scaling, top_k, 0,
-                 nullptr, nullptr, nullptr, out_w, out_ids};
+                 nullptr, nullptr, nullptr, out_w, out_ids, logit_dtype};
   return cuda_status(launch_router(experts, scoring, 0, p, (cudaStream_t)stream), "exf_router_topk");
 }
 
-EXF_API int exf_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
-                            int scoring, const void* token_ids, int id_dtype,
+EXF_API int exf_router_hash(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                            int top_k, int scoring, const void* token_ids, int id_dtype,
                             const int32_t* table, int64_t table_rows, int renormalize,
                             float scaling, float* out_w, int32_t* out_ids, exf_stream_t stream) {
   const char* name = "exf_router_hash";
@@ -126,6 +127,7 @@ EXF_API int exf_router_hash(const float* logits, int64_t tokens, int experts, in
   EXF_REQUIRE(top_k >= 1 && top_k <= 8, "%s: top_k must be in [1, 8], got %d", name, top_k);
   EXF_REQUIRE(experts >= 1, "%s: experts must be >= 1", name);
   EXF_REQUIRE(good_idtype(id_dtype), "%s: unsupported token id dtype", name);
+  EXF_REQUIRE(good_wdtype(logit_dtype), "%s: logits must be EXF_F32, EXF_BF16 or EXF_F16", name);
   EXF_REQUIRE(table_rows >= 1, "%s: the hash table needs at least one row", name);
   if (scoring == EXF_SOFTMAX)
     return fail(EXF_ERR_UNSUPPORTED, "%s: hash routing takes sigmoid or sqrtsoftplus scores", name);
@@ -133,20 +135,23 @@ EXF_API int exf_router_hash(const float* logits, int64_t tokens, int experts, in
               name, scoring);
   if (tokens == 0) return EXF_OK;
   EXF_REQUIRE(logits && token_ids && table && out_w && out_ids, "%s: null pointer", name);
-  return cuda_status(launch_router_hash(logits, tokens, experts, top_k, scoring, token_ids,
+  return cuda_status(launch_router_hash(logits, logit_dtype, tokens, experts, top_k, scoring,
+                                        token_ids,
                                         id_dtype, table, table_rows, renormalize, scaling, out_w,
                                         out_ids, (cudaStream_t)stream),
                      name);
 }
 
-EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int layers, int experts,
-                                    int top_k, int scoring, const float* bias, int renormalize,
+EXF_API int exf_router_fold_prefill(const void* logits, int logit_dtype, int64_t tokens,
+                                    int layers, int experts, int top_k, int scoring,
+                                    const float* bias, int renormalize,
                                     float scaling, int target_k, int variant, int renorm_mode,
                                     const float* coeff, const float* sel_loss,
                                     const float* conf_loss, float* out_w, int32_t* out_ids,
                                     exf_stream_t stream) {
   const char* name = "exf_router_fold_prefill";
-  int rc = router_common(name, logits, tokens, layers, experts, top_k, scoring, out_w, out_ids);
+  int rc = router_common(name, logits, logit_dtype, tokens, layers, experts, top_k, scoring,
+                         out_w, out_ids);
   if (rc != EXF_OK) return rc;
   EXF_REQUIRE(variant == EXF_QWEN3 || variant == EXF_DSV4, "%s: unknown variant %d", name, variant);
   EXF_REQUIRE(target_k >= 1 && target_k <= top_k, "%s: target_k must be in [1, top_k]", name);
@@ -157,7 +162,7 @@ EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int lay
   EXF_REQUIRE(renorm_mode != 2 || conf_loss, "%s: similarity_blend needs conf_loss", name);
   EXF_REQUIRE(!bias || aligned16(bias), "%s: bias must be 16-byte aligned", name);
   RouterParams p{logits, tokens, layers, top_k, bias, renormalize, scaling, target_k, renorm_mode,
-                 coeff, sel_loss, conf_loss, out_w, out_ids};
+                 coeff, sel_loss, conf_loss, out_w, out_ids, logit_dtype};
   return cuda_status(launch_router(experts, scoring, variant == EXF_QWEN3 ? 1 : 2, p,
                                    (cudaStream_t)stream),
                      name);

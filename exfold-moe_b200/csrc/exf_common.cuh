@@ -148,6 +148,49 @@ __device__ __forceinline__ long long fixed_point(float p) {
   return __float2ll_rn(__fmul_rn(p, 4294967296.0f));
 }
 
+// ---------------------------------------------------------------------------------------------
+// Router logits come as fp32, bf16 or fp16 (the model's gate output dtype).  Each logit is
+// converted to fp32 exactly (bf16: the 16 bits become the high half of the float; fp16: the
+// exact half-to-float conversion), and selection and weights run on the converted values, so the
+// results equal the fp32 path on logits.float().  Four consecutive logits are 16 bytes (fp32) or
+// 8 bytes (16-bit): one load either way.
+template <typename LT>
+__device__ __forceinline__ float logit_f32(LT v);
+template <>
+__device__ __forceinline__ float logit_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float logit_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __uint_as_float(static_cast<uint32_t>(__bfloat16_as_ushort(v)) << 16);
+}
+template <>
+__device__ __forceinline__ float logit_f32<__half>(__half v) { return __half2float(v); }
+
+// Two packed 16-bit logits (low half first) as two floats.
+template <typename LT>
+__device__ __forceinline__ float2 logit2_f32(uint32_t u);
+template <>
+__device__ __forceinline__ float2 logit2_f32<__nv_bfloat16>(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+template <>
+__device__ __forceinline__ float2 logit2_f32<__half>(uint32_t u) {
+  return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(u & 0xFFFFu))),
+                     __half2float(__ushort_as_half(static_cast<unsigned short>(u >> 16))));
+}
+
+// logits p[0..3] as a float4; p is 16-byte (fp32) / 8-byte (16-bit) aligned.  Plain load (global
+// or shared memory).
+template <typename LT>
+__device__ __forceinline__ float4 load_logits4(const LT* p) {
+  if constexpr (sizeof(LT) == 4) {
+    return *reinterpret_cast<const float4*>(p);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = logit2_f32<LT>(u.x), b = logit2_f32<LT>(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+}
+
 // Streaming 16-byte load that does not allocate in L1 (router logits are read exactly once).
 __device__ __forceinline__ float4 ld_stream_f4(const float* p) {
   float4 v;
@@ -155,6 +198,20 @@ __device__ __forceinline__ float4 ld_stream_f4(const float* p) {
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "l"(p));
   return v;
+}
+// load_logits4 from global memory through the non-allocating streaming path
+template <typename LT>
+__device__ __forceinline__ float4 ld_stream_logits4(const LT* p) {
+  if constexpr (sizeof(LT) == 4) {
+    return ld_stream_f4(reinterpret_cast<const float*>(p));
+  } else {
+    uint32_t x, y;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+                 : "=r"(x), "=r"(y)
+                 : "l"(p));
+    const float2 a = logit2_f32<LT>(x), b = logit2_f32<LT>(y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
 }
 
 }  // namespace exf

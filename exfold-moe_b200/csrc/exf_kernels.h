@@ -9,7 +9,7 @@ namespace exf {
 enum FoldKind { kFoldNone = 0, kFoldQwen3 = 1, kFoldDsv4 = 2 };
 
 struct RouterParams {
-  const float* logits;   // [layers][tokens][E]
+  const void* logits;    // [layers][tokens][E] of logit_dtype
   int64_t tokens;        // per layer
   int layers;
   int top_k;
@@ -23,6 +23,7 @@ struct RouterParams {
   const float* conf_loss;
   float* out_w;          // [layers][tokens][top_k or target_k]
   int32_t* out_ids;
+  int logit_dtype;       // EXF_F32, EXF_BF16 or EXF_F16
 };
 
 struct FoldParams {
@@ -112,8 +113,8 @@ struct AlignParams {
 };
 
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p, cudaStream_t s);
-cudaError_t launch_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
-                               int scoring, const void* token_ids, int id_dtype,
+cudaError_t launch_router_hash(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                               int top_k, int scoring, const void* token_ids, int id_dtype,
                                const int32_t* table, int64_t table_rows, int renormalize,
                                float scaling, float* out_w, int32_t* out_ids, cudaStream_t s);
 // One token per thread, bulk-copied tiles: 128 experts, softmax, top-8, renormalised, Qwen3 fold

@@ -6,11 +6,14 @@
 // optionally fused with the ExFold prefill fold (exfold/deepseek_v4/csrc/exfold_kernels.cu:17-118:
 // stable sort by weight, each omitted route folded onto the retained expert of smallest selection
 // loss, renorm modes 0/1/2).
-//   * Tiles of 16 tokens x 1 KB stream through a ring of shared-memory slots filled by bulk
-//     copies (cp.async.bulk, mbarrier completion) and shared by the CTA's 8 warps, as in
-//     router_tpt.cu.  A warp takes two tiles (A, B) at a time.  For the group maxima, lanes 2r
-//     and 2r+1 split token r of a tile: lane half h reads columns 128h..128h+127 in the 16-byte
-//     chunk order i ^ (lane & 7), so the 8 lanes of a quarter-warp hit 8 different bank quads.
+//   * Tiles of 16 tokens x 1 KB (fp32 logits; 512 B rows of bf16 / fp16 logits, twice the
+//     slots) stream through a ring of shared-memory slots filled by bulk copies (cp.async.bulk,
+//     mbarrier completion) and shared by the CTA's 8 warps, as in router_tpt.cu.  A warp takes
+//     two tiles (A, B) at a time.  For the group maxima, lanes 2r and 2r+1 split token r of a
+//     tile: lane half h reads the 32 groups of columns 128h..128h+127 in the chunk order
+//     u ^ (lane & 7) (16-byte fp32 chunks) or u ^ (lane & 15) (8-byte 16-bit chunks), so the
+//     lanes of each quarter-warp / half-warp hit different banks.  16-bit logits are converted
+//     to fp32 exactly on load.
 //     Everything after that is per token with one lane each: lane 2r ranks token r of A, lane
 //     2r+1 token r of B.
 //   * Approximate scores a~ = 0.5 tanh.approx(x / 2) + (0.5 + bias): one MUFU operation per
@@ -50,17 +53,20 @@ constexpr int kE = 256;
 constexpr int kK = 8;
 constexpr int kWarps = 8;                // warps per CTA, each ranking two tiles at a time
 constexpr int kRows = 16;                // tokens per tile
-constexpr int kTileFloats = kRows * kE;  // 16 KB
 
 // |approximate - exact score| <= kErrAbs + kErrRel |score| (see the header comment).
 constexpr float kErrAbs = 1.0e-5f;
 constexpr float kErrRel = 4.0e-7f;
 
-template <int FOLD>
+template <int FOLD, typename LT>
 struct BiasedSmem {
-  // the fold's 128 KB table leaves room for 6 slots; without it, 13
-  static constexpr int kSlots = FOLD == kFoldNone ? 13 : 6;
-  float tile[kSlots][kTileFloats];
+  // 16 KB tiles of fp32 logits (8 KB of bf16 / fp16): the fold's 128 KB table leaves room for 6
+  // (12), without it 13 (26)
+  static constexpr int kSlots = (FOLD == kFoldNone ? 13 : 6) * (4 / sizeof(LT));
+  // group chunk order of lane t: u ^ (t & kSwz) (16-byte fp32 chunks: quarter-warps, 8-byte
+  // 16-bit chunks: half-warps hit distinct banks)
+  static constexpr uint32_t kSwz = sizeof(LT) == 4 ? 7u : 15u;
+  LT tile[kSlots][kRows * kE];
   uint16_t loss_hi[FOLD == kFoldNone ? 8 : kE * kE];  // high 16 bits of each loss
   float cterm[kE];         // 0.5 + bias (rounded), the constant of the approximate score
   float bias[kE];          // the current layer's bias (zeros without one)
@@ -70,10 +76,24 @@ struct BiasedSmem {
   int next;                // next tile of the current layer to hand out
   int failed;              // a wait timed out: the remaining tiles are marked, not ranked
 };
-template <int FOLD>
-constexpr size_t biased_smem_bytes() { return sizeof(BiasedSmem<FOLD>); }
-static_assert(biased_smem_bytes<kFoldDsv4>() <= 232448, "router_biased: shared memory");
-static_assert(biased_smem_bytes<kFoldNone>() <= 232448, "router_biased: shared memory");
+template <int FOLD, typename LT>
+constexpr size_t biased_smem_bytes() { return sizeof(BiasedSmem<FOLD, LT>); }
+static_assert(biased_smem_bytes<kFoldDsv4, float>() <= 232448, "router_biased: shared memory");
+static_assert(biased_smem_bytes<kFoldNone, float>() <= 232448, "router_biased: shared memory");
+static_assert(biased_smem_bytes<kFoldDsv4, __half>() <= 232448, "router_biased: shared memory");
+static_assert(biased_smem_bytes<kFoldNone, __half>() <= 232448, "router_biased: shared memory");
+
+// 4 logits from global memory through the read-only path, as floats
+template <typename LT>
+__device__ __forceinline__ float4 ldg_logits4(const LT* p) {
+  if constexpr (sizeof(LT) == 4) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+  } else {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = logit2_f32<LT>(u.x), b = logit2_f32<LT>(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+}
 
 __device__ __forceinline__ float tanh_approx(float x) {
   float r;
@@ -142,7 +162,8 @@ __device__ __forceinline__ void sort8p(uint64_t (&v)[kK], float (&s)[kK]) {
 
 // Exact top 8 of one row by insertion of every element whose approximate score reaches bound
 // (or is NaN); every element when all is set.  Out of line: rarely taken.
-__device__ __noinline__ void exact_top8_biased(const float* grow, const float* cterm,
+template <typename LT>
+__device__ __noinline__ void exact_top8_biased(const LT* grow, const float* cterm,
                                                const float* bias, float bound, bool all,
                                                uint64_t* out, float* out_s) {
   uint64_t T[kK];
@@ -156,7 +177,7 @@ __device__ __noinline__ void exact_top8_biased(const float* grow, const float* c
   for (int c0 = 0; c0 < kE / 4; c0 += 8) {
     float4 xs[8];  // 8 chunks in flight
 #pragma unroll
-    for (int u = 0; u < 8; ++u) xs[u] = __ldg(reinterpret_cast<const float4*>(grow) + c0 + u);
+    for (int u = 0; u < 8; ++u) xs[u] = ldg_logits4(grow + 4 * (c0 + u));
 #pragma unroll 1
     for (int u = 0; u < 8; ++u) {
       const int c = c0 + u;
@@ -179,16 +200,17 @@ __device__ __noinline__ void exact_top8_biased(const float* grow, const float* c
   }
 }
 
-template <int FOLD, int P>
+template <int FOLD, int P, typename LT>
 __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const RouterParams p) {
-  using Smem = BiasedSmem<FOLD>;
+  using Smem = BiasedSmem<FOLD, LT>;
   constexpr int kSlots = Smem::kSlots;
   extern __shared__ __align__(128) uint8_t biased_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(biased_raw);
+  const LT* logits = static_cast<const LT*>(p.logits);
   const int t = threadIdx.x & 31;
   const int h = t & 1;         // column half of this lane in the group maxima; tile B after it
   const int r = t >> 1;        // token of the tile
-  const int sw = t & 7;        // chunk order of this lane
+  const uint32_t swz = static_cast<uint32_t>(t) & Smem::kSwz;  // chunk order of this lane
   const int64_t tokens = p.tokens;
   // Tiles never straddle a layer (the last one of a layer may be short): global tile g is tile
   // g % tpl of layer g / tpl.  This CTA ranks the contiguous range [g0, g0 + nk).
@@ -203,9 +225,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
     const int slot = static_cast<int>(k % kSlots);
     const int64_t l = (g0 + k) / tpl, tl = (g0 + k) - l * tpl;
     const int64_t rows = tokens - tl * kRows < kRows ? tokens - tl * kRows : kRows;
-    const uint32_t bytes = static_cast<uint32_t>(rows * kE * sizeof(float));
+    const uint32_t bytes = static_cast<uint32_t>(rows * kE * sizeof(LT));
     bar_expect(&sm.bar[slot], bytes);
-    bulk_load(sm.tile[slot], p.logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
+    bulk_load(sm.tile[slot], logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
   };
   // Launched as a programmatic dependent of the previous kernel in the stream.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -248,13 +270,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
     // approximate group maxima, keyed: the only reads of the tile
     uint32_t g[32];
     if (ok) {
-      const float* rowp = sm.tile[slot] + rowi * kE;
+      const LT* rowp = sm.tile[slot] + rowi * kE;
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int c = 32 * h + 8 * s + (i ^ sw);
-          const float4 v = *reinterpret_cast<const float4*>(rowp + 4 * c);
+          const int c = 32 * h + static_cast<int>(static_cast<uint32_t>(8 * s + i) ^ swz);
+          const float4 v = load_logits4(rowp + 4 * c);
           const float4 cc = *reinterpret_cast<const float4*>(sm.cterm + 4 * c);
           const float m = fmax_nan(fmax_nan(approx_biased(v.x, cc.x), approx_biased(v.y, cc.y)),
                                    fmax_nan(approx_biased(v.z, cc.z), approx_biased(v.w, cc.w)));
@@ -349,7 +371,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       const bool use_b = h && has_b;
       const bool valid = use_b ? tok_b + r < tokens : (h == 0 && tok_a + r < tokens);
       const int64_t orow = l * tokens + (use_b ? tok_b : tok_a) + r;
-      const float* grow = p.logits + (l * tokens + (use_b ? tok_b + rb : tok_a + ra)) * kE;
+      const LT* grow = logits + (l * tokens + (use_b ? tok_b + rb : tok_a + ra)) * kE;
       uint32_t pk[kK];
 #pragma unroll
       for (int q = 0; q < kK; ++q) pk[q] = use_b ? pkb[q] : pka[q];
@@ -378,9 +400,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       for (int q = 0; q < kK; ++q) {
         const uint32_t id = 63u - (pk[q] & 63u);
         const uint32_t hh = id >> 5, i = id & 31u;
-        const uint32_t osw = (static_cast<uint32_t>(t) & 6u) | hh;  // chunk order of its lane
-        cq[q] = static_cast<int>(32 * hh + 8 * (i >> 3) + ((i & 7u) ^ osw));
-        xq[q] = __ldg(reinterpret_cast<const float4*>(grow) + cq[q]);
+        // chunk order of the lane (of this lane's pair) that took the maximum
+        const uint32_t osw = (static_cast<uint32_t>(t) & (Smem::kSwz & ~1u)) | hh;
+        cq[q] = static_cast<int>(32 * hh + (i ^ osw));
+        xq[q] = ldg_logits4(grow + 4 * cq[q]);
       }
 #pragma unroll
       for (int q = 0; q < kK; ++q) {
@@ -436,9 +459,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
         if (!(g9 < bound)) {
           const uint32_t id = 63u - (p9 & 63u);
           const uint32_t hh = id >> 5, i = id & 31u;
-          const uint32_t osw = (static_cast<uint32_t>(t) & 6u) | hh;
-          const int c = static_cast<int>(32 * hh + 8 * (i >> 3) + ((i & 7u) ^ osw));
-          const float4 x = __ldg(reinterpret_cast<const float4*>(grow) + c);
+          const uint32_t osw = (static_cast<uint32_t>(t) & (Smem::kSwz & ~1u)) | hh;
+          const int c = static_cast<int>(32 * hh + (i ^ osw));
+          const float4 x = ldg_logits4(grow + 4 * c);
           const float4 cc = *reinterpret_cast<const float4*>(sm.cterm + 4 * c);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -452,7 +475,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       } else {
         uint64_t Te[kK];
         float Se[kK];
-        exact_top8_biased(grow, sm.cterm, sm.bias, bound, nonfinite, Te, Se);
+        exact_top8_biased<LT>(grow, sm.cterm, sm.bias, bound, nonfinite, Te, Se);
 #pragma unroll
         for (int q = 0; q < kK; ++q) {
           T[q] = Te[q];
@@ -613,10 +636,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
   }
 }
 
-template <int FOLD, int P>
-cudaError_t launch_biased(const RouterParams& p, cudaStream_t stream) {
-  auto kern = router_biased_kernel<FOLD, P>;
-  constexpr size_t smem = biased_smem_bytes<FOLD>();
+template <int FOLD, int P, typename LT>
+cudaError_t launch_biased_l(const RouterParams& p, cudaStream_t stream) {
+  auto kern = router_biased_kernel<FOLD, P, LT>;
+  constexpr size_t smem = biased_smem_bytes<FOLD, LT>();
   static std::mutex mu;
   static bool allowed[64] = {};
   int dev = 0;
@@ -648,6 +671,15 @@ cudaError_t launch_biased(const RouterParams& p, cudaStream_t stream) {
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, p);
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int FOLD, int P>
+cudaError_t launch_biased(const RouterParams& p, cudaStream_t stream) {
+  switch (p.logit_dtype) {
+    case EXF_F32: return launch_biased_l<FOLD, P, float>(p, stream);
+    case EXF_BF16: return launch_biased_l<FOLD, P, __nv_bfloat16>(p, stream);
+    default: return launch_biased_l<FOLD, P, __half>(p, stream);
+  }
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }

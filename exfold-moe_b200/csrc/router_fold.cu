@@ -3,7 +3,8 @@
 // router_kernel: one pass over the router logits per token, optionally fused with the ExFold
 // prefill fold, so the [tokens][top_k] routing tensors never reach HBM.
 //   * A token is owned by a group of L = E/32 lanes; each lane holds 32 logits in registers
-//     (8 coalesced 16-byte streaming loads) and stages them in shared memory.
+//     (8 coalesced streaming loads of 4 logits: 16 bytes fp32, 8 bytes bf16 / fp16, converted to
+//     fp32 exactly) and stages them in shared memory as fp32.
 //   * Selection: the exact top-k set is contained in the candidates whose key is >= theta, where
 //     theta is the k-th largest maximum over groups of 4 consecutive keys (k distinct elements
 //     reach it, so the k-th largest key is >= theta).  theta comes from a register bitonic
@@ -82,9 +83,10 @@ struct __align__(16) RouterSmem {
   __align__(16) float acc[S::WARPS][S::TPW][SSTR];  // folded retained weights
 };
 
-template <int E, int SCORING, int FOLD>
+template <int E, int SCORING, int FOLD, typename LT>
 __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
     router_kernel(const RouterParams p) {
+  const LT* logits = static_cast<const LT*>(p.logits);
   using S = RouterShape<E>;
   constexpr int L = S::L;
   constexpr int TPW = S::TPW;
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
   float4 nv[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    nv[i] = gt < total ? ld_stream_f4(p.logits + gt * E + 4 * (r + L * i))
+    nv[i] = gt < total ? ld_stream_logits4(logits + gt * E + 4 * (r + L * i))
                        : make_float4(0.f, 0.f, 0.f, 0.f);
 
   for (int64_t base = gt - g; base < total; base += stride, gt += stride) {
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(RouterShape<E>::WARPS * 32)
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        nv[i] = ngt < total ? ld_stream_f4(p.logits + ngt * E + 4 * (r + L * i))
+        nv[i] = ngt < total ? ld_stream_logits4(logits + ngt * E + 4 * (r + L * i))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncwarp();
@@ -598,9 +600,9 @@ __global__ void __launch_bounds__(256) fold_kernel(const FoldParams p) {
 // sqrtsoftplus divisor clamped at 1e-20) and scaled.  One thread per token.  A token id outside
 // the table gives ids -1 and weights 0; a table entry outside [0, experts) keeps its id and
 // gets weight 0, so nothing is read out of range.
-template <int SCORING, typename TID>
+template <int SCORING, typename TID, typename LT>
 __global__ void __launch_bounds__(256) router_hash_kernel(
-    const float* logits, int64_t tokens, int E, int K, const TID* token_ids, const int32_t* table,
+    const LT* logits, int64_t tokens, int E, int K, const TID* token_ids, const int32_t* table,
     int64_t rows, int renormalize, float scaling, float* out_w, int32_t* out_ids) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= tokens) return;
@@ -615,7 +617,7 @@ __global__ void __launch_bounds__(256) router_hash_kernel(
     return;
   }
   const int32_t* trow = table + tid * K;
-  const float* xrow = logits + t * E;
+  const LT* xrow = logits + t * E;
   float w[kMaxK];
   int id[kMaxK];
   float sum = 0.0f;
@@ -624,7 +626,7 @@ __global__ void __launch_bounds__(256) router_hash_kernel(
     if (s < K) {
       const int e = __ldg(trow + s);
       id[s] = e;
-      w[s] = (e >= 0 && e < E) ? exact_score<SCORING>(__ldg(xrow + e)) : 0.0f;
+      w[s] = (e >= 0 && e < E) ? exact_score<SCORING>(logit_f32<LT>(xrow[e])) : 0.0f;
       sum = __fadd_rn(sum, w[s]);
     }
   }
@@ -640,44 +642,68 @@ __global__ void __launch_bounds__(256) router_hash_kernel(
   }
 }
 
-template <int SCORING, typename TID>
-static cudaError_t launch_hash_t(const float* logits, int64_t tokens, int E, int K,
+template <int SCORING, typename TID, typename LT>
+static cudaError_t launch_hash_t(const void* logits, int64_t tokens, int E, int K,
                                  const void* token_ids, const int32_t* table, int64_t rows,
                                  int renormalize, float scaling, float* out_w, int32_t* out_ids,
                                  cudaStream_t stream) {
   const unsigned blocks = (unsigned)((tokens + 255) / 256);
-  router_hash_kernel<SCORING, TID><<<blocks, 256, 0, stream>>>(
-      logits, tokens, E, K, static_cast<const TID*>(token_ids), table, rows, renormalize, scaling,
-      out_w, out_ids);
+  router_hash_kernel<SCORING, TID, LT><<<blocks, 256, 0, stream>>>(
+      static_cast<const LT*>(logits), tokens, E, K, static_cast<const TID*>(token_ids), table,
+      rows, renormalize, scaling, out_w, out_ids);
   return cudaGetLastError();
 }
 
-cudaError_t launch_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
-                               int scoring, const void* token_ids, int id_dtype,
+template <int SCORING, typename LT>
+static cudaError_t launch_hash_l(const void* logits, int64_t tokens, int E, int K,
+                                 const void* token_ids, int id_dtype, const int32_t* table,
+                                 int64_t rows, int renormalize, float scaling, float* out_w,
+                                 int32_t* out_ids, cudaStream_t s) {
+  return id_dtype == EXF_I32
+             ? launch_hash_t<SCORING, int32_t, LT>(logits, tokens, E, K, token_ids, table, rows,
+                                                   renormalize, scaling, out_w, out_ids, s)
+             : launch_hash_t<SCORING, int64_t, LT>(logits, tokens, E, K, token_ids, table, rows,
+                                                   renormalize, scaling, out_w, out_ids, s);
+}
+
+template <int SCORING>
+static cudaError_t launch_hash_s(const void* logits, int logit_dtype, int64_t tokens, int E,
+                                 int K, const void* token_ids, int id_dtype, const int32_t* table,
+                                 int64_t rows, int renormalize, float scaling, float* out_w,
+                                 int32_t* out_ids, cudaStream_t s) {
+  switch (logit_dtype) {
+    case EXF_F32:
+      return launch_hash_l<SCORING, float>(logits, tokens, E, K, token_ids, id_dtype, table, rows,
+                                           renormalize, scaling, out_w, out_ids, s);
+    case EXF_BF16:
+      return launch_hash_l<SCORING, __nv_bfloat16>(logits, tokens, E, K, token_ids, id_dtype,
+                                                   table, rows, renormalize, scaling, out_w,
+                                                   out_ids, s);
+    default:
+      return launch_hash_l<SCORING, __half>(logits, tokens, E, K, token_ids, id_dtype, table,
+                                            rows, renormalize, scaling, out_w, out_ids, s);
+  }
+}
+
+cudaError_t launch_router_hash(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                               int top_k, int scoring, const void* token_ids, int id_dtype,
                                const int32_t* table, int64_t table_rows, int renormalize,
                                float scaling, float* out_w, int32_t* out_ids, cudaStream_t s) {
-  const bool i32 = id_dtype == EXF_I32;
   if (scoring == EXF_SQRTSOFTPLUS)
-    return i32 ? launch_hash_t<EXF_SQRTSOFTPLUS, int32_t>(logits, tokens, experts, top_k, token_ids,
-                                                          table, table_rows, renormalize, scaling,
-                                                          out_w, out_ids, s)
-               : launch_hash_t<EXF_SQRTSOFTPLUS, int64_t>(logits, tokens, experts, top_k, token_ids,
-                                                          table, table_rows, renormalize, scaling,
-                                                          out_w, out_ids, s);
-  return i32 ? launch_hash_t<EXF_SIGMOID, int32_t>(logits, tokens, experts, top_k, token_ids, table,
-                                                   table_rows, renormalize, scaling, out_w,
-                                                   out_ids, s)
-             : launch_hash_t<EXF_SIGMOID, int64_t>(logits, tokens, experts, top_k, token_ids, table,
-                                                   table_rows, renormalize, scaling, out_w,
-                                                   out_ids, s);
+    return launch_hash_s<EXF_SQRTSOFTPLUS>(logits, logit_dtype, tokens, experts, top_k, token_ids,
+                                           id_dtype, table, table_rows, renormalize, scaling,
+                                           out_w, out_ids, s);
+  return launch_hash_s<EXF_SIGMOID>(logits, logit_dtype, tokens, experts, top_k, token_ids,
+                                    id_dtype, table, table_rows, renormalize, scaling, out_w,
+                                    out_ids, s);
 }
 
 // ---------------------------------------------------------------------------------------------
 // Host launchers
-template <int E, int SCORING, int FOLD>
-static cudaError_t launch_router_e(const RouterParams& p, cudaStream_t stream) {
+template <int E, int SCORING, int FOLD, typename LT>
+static cudaError_t launch_router_l(const RouterParams& p, cudaStream_t stream) {
   using S = RouterShape<E>;
-  auto kern = router_kernel<E, SCORING, FOLD>;
+  auto kern = router_kernel<E, SCORING, FOLD, LT>;
   const int64_t total = (int64_t)p.layers * p.tokens;
   const int64_t per_block = (int64_t)S::WARPS * S::TPW;
   int64_t blocks = (total + per_block - 1) / per_block;
@@ -686,6 +712,15 @@ static cudaError_t launch_router_e(const RouterParams& p, cudaStream_t stream) {
   if (blocks < 1) blocks = 1;
   kern<<<(unsigned)blocks, S::WARPS * 32, 0, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <int E, int SCORING, int FOLD>
+static cudaError_t launch_router_e(const RouterParams& p, cudaStream_t stream) {
+  switch (p.logit_dtype) {
+    case EXF_F32: return launch_router_l<E, SCORING, FOLD, float>(p, stream);
+    case EXF_BF16: return launch_router_l<E, SCORING, FOLD, __nv_bfloat16>(p, stream);
+    default: return launch_router_l<E, SCORING, FOLD, __half>(p, stream);
+  }
 }
 
 template <int SCORING, int FOLD>

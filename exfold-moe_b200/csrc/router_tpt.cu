@@ -51,12 +51,18 @@ constexpr int kK = 8;
 #define EXF_TPT_SLOTS 10
 #endif
 constexpr int kWarps = EXF_TPT_WARPS;    // warps per CTA, each ranking one tile at a time
-constexpr int kSlots = EXF_TPT_SLOTS;    // tile slots per CTA: a ring shared by its warps
 constexpr int kRows = 32;                // tokens per tile: one per lane
-constexpr int kTileFloats = kRows * kE;  // 16 KB
 
+// Tile slots per CTA (a ring shared by its warps): 16 KB tiles of fp32 logits, 8 KB of bf16 /
+// fp16 logits, so the 16-bit ring has twice the slots in the same shared memory.
+template <typename LT>
 struct TptSmem {
-  float tile[kSlots][kTileFloats];
+  static constexpr int kSlots = sizeof(LT) == 4 ? EXF_TPT_SLOTS : 2 * EXF_TPT_SLOTS;
+  // Lane t reads the 16-byte (fp32) / 8-byte (16-bit) group chunks of its row in the order
+  // u ^ (t & kSwz): rows are 512 / 256 bytes apart, so each quarter-warp (16-byte loads) or
+  // half-warp (8-byte loads) hits distinct banks.
+  static constexpr int kSwz = sizeof(LT) == 4 ? 7 : 15;
+  LT tile[kSlots][kRows * kE];
   float loss[kE * kE];     // the current layer's selection-loss table (fold only)
   uint64_t bar[kSlots];    // tile copies
   uint64_t tbar;           // table copies
@@ -65,20 +71,25 @@ struct TptSmem {
   int next;                // next tile of the current layer to hand out
   int failed;              // a wait timed out: the remaining tiles are marked, not ranked
 };
-constexpr size_t kTptSmemBytes = sizeof(TptSmem) + 128;  // + alignment slack
-static_assert(kTptSmemBytes <= 232448, "router_tpt: shared memory over the per-CTA limit");
+template <typename LT>
+constexpr size_t tpt_smem_bytes() {
+  return sizeof(TptSmem<LT>) + 128;  // + alignment slack
+}
+static_assert(tpt_smem_bytes<float>() <= 232448, "router_tpt: shared memory over the limit");
+static_assert(tpt_smem_bytes<__nv_bfloat16>() <= 232448, "router_tpt: shared memory over the limit");
 
 // Exact top 8 of one row by insertion of every element (key at least lb) of every group whose
 // maximum reaches lb; -0 ranks equal to +0.  Out of line: rarely taken, and kept out of the
 // instruction cache of the hot loop.
-__device__ __noinline__ void exact_top8(const float* rowp, int sw, uint32_t lb, uint64_t* out) {
+template <typename LT>
+__device__ __noinline__ void exact_top8(const LT* rowp, int swz, uint32_t lb, uint64_t* out) {
   uint64_t T[kK];
 #pragma unroll
   for (int q = 0; q < kK; ++q) T[q] = 0;
 #pragma unroll 1
   for (int u = 0; u < 32; ++u) {
-    const int cbase = 32 * (u >> 3) + 4 * ((u & 7) ^ sw);
-    const float4 v = *reinterpret_cast<const float4*>(rowp + cbase);
+    const int cbase = 4 * (u ^ swz);
+    const float4 v = load_logits4(rowp + cbase);
     const uint32_t k[4] = {key_of(v.x), key_of(v.y), key_of(v.z), key_of(v.w)};
     if (max(max(k[0], k[1]), max(k[2], k[3])) < lb) continue;
 #pragma unroll
@@ -89,13 +100,16 @@ __device__ __noinline__ void exact_top8(const float* rowp, int sw, uint32_t lb, 
   for (int q = 0; q < kK; ++q) out[q] = T[q];
 }
 
-template <int FOLD, int P>
+template <int FOLD, int P, typename LT>
 __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const RouterParams p) {
   extern __shared__ uint8_t tpt_raw[];
-  TptSmem& sm = *reinterpret_cast<TptSmem*>((reinterpret_cast<uintptr_t>(tpt_raw) + 127) &
-                                            ~static_cast<uintptr_t>(127));
+  using Smem = TptSmem<LT>;
+  constexpr int kSlots = Smem::kSlots;
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(tpt_raw) + 127) &
+                                      ~static_cast<uintptr_t>(127));
+  const LT* logits = static_cast<const LT*>(p.logits);
   const int t = threadIdx.x & 31;
-  const int sw = t & 7;
+  const int swz = t & Smem::kSwz;
   const int64_t tokens = p.tokens;
   // Tiles never straddle a layer (the last one of a layer may be short): global tile g is tile
   // g % tpl of layer g / tpl.  This CTA ranks the contiguous range [g0, g0 + nk), so it crosses
@@ -111,9 +125,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
     const int slot = static_cast<int>(k % kSlots);
     const int64_t l = (g0 + k) / tpl, tl = (g0 + k) - l * tpl;
     const int64_t rows = tokens - tl * kRows < kRows ? tokens - tl * kRows : kRows;
-    const uint32_t bytes = static_cast<uint32_t>(rows * kE * sizeof(float));
+    const uint32_t bytes = static_cast<uint32_t>(rows * kE * sizeof(LT));
     bar_expect(&sm.bar[slot], bytes);
-    bulk_load(sm.tile[slot], p.logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
+    bulk_load(sm.tile[slot], logits + (l * tokens + tl * kRows) * kE, bytes, &sm.bar[slot]);
   };
   // Launched as a programmatic dependent of the previous kernel in the stream: let the next
   // launch's CTAs take SMs as this grid's CTAs exit, and wait here until the previous grid has
@@ -193,12 +207,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
       const int64_t tok = (g0 + k - l * tpl) * kRows + t;
       const bool valid = tok < tokens;
       const int64_t row = l * tokens + tok;
-      float* rowp = sm.tile[slot] + t * kE;
+      const LT* rowp = sm.tile[slot] + t * kE;
       uint64_t T[kK];
 
       // ======== phase 1: the selection, the only part that reads the tile =====================
       if (ok) {
-        // ---- group maxima (slot u = 8 s + i holds columns 32 s + 4 (i ^ sw) .. + 3) ---------
+        // ---- group maxima (slot u holds columns 4 (u ^ swz) .. + 3) ---------------------------
         // A float maximum keyed once equals the key maximum except that -0 may stand for +0
         // (harmless: zeros never reach the fast path's theta, and the exact path merges them);
         // a NaN makes the group's key all ones, which the exact path below takes over.  The key
@@ -208,7 +222,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
         for (int s = 0; s < 4; ++s)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 v = *reinterpret_cast<const float4*>(rowp + 32 * s + 4 * (i ^ sw));
+            const float4 v = load_logits4(rowp + 4 * ((8 * s + i) ^ swz));
             const uint32_t g = order_key(fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
             pk[8 * s + i] = (g & ~31u) | (31u - (8 * s + i));
           }
@@ -227,8 +241,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
 #pragma unroll
         for (int i = 0; i < kK; ++i) {
           const uint32_t u = 31u - (pk[i] & 31u);
-          cb[i] = 32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw);
-          const float4 v = *reinterpret_cast<const float4*>(rowp + cb[i]);
+          cb[i] = 4 * static_cast<int>(u ^ static_cast<uint32_t>(swz));
+          const float4 v = load_logits4(rowp + cb[i]);
           ek[i][0] = order_key(v.x);
           ek[i][1] = order_key(v.y);
           ek[i][2] = order_key(v.z);
@@ -269,15 +283,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
             xm &= xm - 1;
             const int i = site >> 2;
             const uint32_t u = (i < 6 ? slo >> (5 * i) : shi >> (5 * (i - 6))) & 31u;
-            const int col =
-                32 * static_cast<int>(u >> 3) + 4 * static_cast<int>((u & 7u) ^ sw) + (site & 3);
-            insert8(T, pack(order_key(rowp[col]), col));
+            const int col = 4 * static_cast<int>(u ^ static_cast<uint32_t>(swz)) + (site & 3);
+            insert8(T, pack(order_key(logit_f32<LT>(rowp[col])), col));
           }
         } else if (valid) {
           // exact insertion over every element of every group whose maximum reaches the bound
           // (pk[7] truncated is below the 8th largest key); a row with a NaN inserts every element
           uint64_t Te[kK];
-          exact_top8(rowp, sw, nan_row ? 0u : pk[kK - 1] & ~31u, Te);
+          exact_top8<LT>(rowp, swz, nan_row ? 0u : pk[kK - 1] & ~31u, Te);
 #pragma unroll
           for (int q = 0; q < kK; ++q) T[q] = Te[q];
         }
@@ -405,9 +418,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
   }
 }
 
-template <int FOLD, int P>
-cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
-  auto kern = router_tpt_kernel<FOLD, P>;
+template <int FOLD, int P, typename LT>
+cudaError_t launch_tpt_l(const RouterParams& p, cudaStream_t stream) {
+  auto kern = router_tpt_kernel<FOLD, P, LT>;
+  constexpr size_t smem = tpt_smem_bytes<LT>();
   static std::mutex mu;
   static bool allowed[64] = {};
   int dev = 0;
@@ -418,7 +432,7 @@ cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
     std::lock_guard<std::mutex> lock(mu);
     if (!allowed[dev]) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kTptSmemBytes));
+                               static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       allowed[dev] = true;
     }
@@ -430,7 +444,7 @@ cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(blocks));
   cfg.blockDim = dim3(kWarps * 32);
-  cfg.dynamicSmemBytes = kTptSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -439,6 +453,15 @@ cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, p);
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int FOLD, int P>
+cudaError_t launch_tpt(const RouterParams& p, cudaStream_t stream) {
+  switch (p.logit_dtype) {
+    case EXF_F32: return launch_tpt_l<FOLD, P, float>(p, stream);
+    case EXF_BF16: return launch_tpt_l<FOLD, P, __nv_bfloat16>(p, stream);
+    default: return launch_tpt_l<FOLD, P, __half>(p, stream);
+  }
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }

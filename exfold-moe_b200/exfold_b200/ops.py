@@ -48,6 +48,13 @@ def _f32c(t: torch.Tensor | None) -> torch.Tensor | None:
     return t.contiguous() if t.dtype == torch.float32 else t.float().contiguous()
 
 
+def _logits_in(t: torch.Tensor) -> torch.Tensor:
+    """Router logits in their own dtype when it is fp32 / bf16 / fp16 (the kernels convert
+    16-bit logits exactly), else as fp32; contiguous and 16-byte aligned."""
+    t = t if t.dtype in _WDT else t.float()
+    return _aligned(t)
+
+
 def _aligned(t: torch.Tensor) -> torch.Tensor:
     t = t.contiguous()
     return t if t.data_ptr() % 16 == 0 else t.clone()
@@ -65,14 +72,16 @@ def _ids_in(ids: torch.Tensor) -> torch.Tensor:
 def router_topk(logits: torch.Tensor, top_k: int, scoring: str = "softmax",
                 bias: torch.Tensor | None = None, renormalize: bool = True,
                 scaling: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
-    """Top-k routing of [tokens, experts] logits -> (weights fp32, ids int32) [tokens, top_k]."""
+    """Top-k routing of [tokens, experts] logits (fp32, bf16 or fp16 natively) -> (weights fp32,
+    ids int32) [tokens, top_k]."""
     dev = _require_cuda(logits, bias)
-    x = _aligned(_f32c(logits))
+    x = _logits_in(logits)
     tokens, experts = x.shape
     b = None if bias is None else _aligned(_f32c(bias))
     w = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
     ids = torch.empty((tokens, top_k), dtype=torch.int32, device=dev)
-    L.check(L.lib().exf_router_topk(x.data_ptr(), tokens, experts, top_k, _SCORING[scoring],
+    L.check(L.lib().exf_router_topk(x.data_ptr(), _WDT[x.dtype], tokens, experts, top_k,
+                                    _SCORING[scoring],
                                     _ptr(b), int(renormalize), float(scaling), w.data_ptr(),
                                     ids.data_ptr(), _stream(dev)))
     return w, ids
@@ -84,7 +93,7 @@ def router_hash(logits: torch.Tensor, token_ids: torch.Tensor, table: torch.Tens
     """Hash routing: routes table[token_ids] (table [rows, top_k], in table order) weighted by
     the unbiased scores of those experts -> (weights fp32, ids int32) [tokens, top_k]."""
     dev = _require_cuda(logits, token_ids, table)
-    x = _f32c(logits)
+    x = _logits_in(logits)
     tokens, experts = x.shape
     tid = _ids_in(token_ids.reshape(-1))
     if tid.numel() != tokens:
@@ -95,7 +104,8 @@ def router_hash(logits: torch.Tensor, token_ids: torch.Tensor, table: torch.Tens
     top_k = tab.shape[1]
     w = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
     ids = torch.empty((tokens, top_k), dtype=torch.int32, device=dev)
-    L.check(L.lib().exf_router_hash(x.data_ptr(), tokens, experts, top_k, _SCORING[scoring],
+    L.check(L.lib().exf_router_hash(x.data_ptr(), _WDT[x.dtype], tokens, experts, top_k,
+                                    _SCORING[scoring],
                                     tid.data_ptr(), _IDT[tid.dtype], tab.data_ptr(), tab.shape[0],
                                     int(renormalize), float(scaling), w.data_ptr(), ids.data_ptr(),
                                     _stream(dev)))
@@ -115,7 +125,7 @@ def router_fold_prefill(logits: torch.Tensor, top_k: int, target_k: int, coeff: 
     (and bias [layers, E]).  Returns (weights fp32, ids int32) [..., tokens, target_k].
     """
     dev = _require_cuda(logits, coeff, sel_loss, bias, conf_loss)
-    x = _aligned(_f32c(logits))
+    x = _logits_in(logits)
     layers = 1 if x.dim() == 2 else x.shape[0]
     tokens, experts = x.shape[-2], x.shape[-1]
     coeff, sel_loss = _f32c(coeff), _f32c(sel_loss)
@@ -128,7 +138,7 @@ def router_fold_prefill(logits: torch.Tensor, top_k: int, target_k: int, coeff: 
     else:
         w, ids = out
     L.check(L.lib().exf_router_fold_prefill(
-        x.data_ptr(), tokens, layers, experts, top_k, _SCORING[scoring], _ptr(b),
+        x.data_ptr(), _WDT[x.dtype], tokens, layers, experts, top_k, _SCORING[scoring], _ptr(b),
         int(renormalize), float(scaling), target_k, _VARIANT[variant], int(renorm_mode),
         coeff.data_ptr(), sel_loss.data_ptr(), _ptr(conf_loss), w.data_ptr(), ids.data_ptr(),
         _stream(dev)))

@@ -61,37 +61,42 @@ EXF_API const char* exf_last_error(void);
 
 /* Router scoring + top-k.  Replaces vLLM fused_topk (softmax; exfold/qwen3/vllm_patch.py:98-109)
  * and fused_topk_bias (sigmoid or sqrtsoftplus + selection bias; exfold/deepseek_v4/
- * vllm_patch.py:175-209).  logits [tokens][experts] fp32, 16-byte aligned; bias [experts] or NULL
+ * vllm_patch.py:175-209).  logits [tokens][experts] of logit_dtype (EXF_F32, EXF_BF16 or EXF_F16:
+ * vLLM hands the router the gate output in the model dtype), 16-byte aligned; 16-bit logits are
+ * converted to fp32 exactly, so the results equal those for logits.float(); bias [experts] or NULL
  * (sigmoid and sqrtsoftplus only).  Slots are ordered by selection key descending, ties by lower
  * expert id.  Weights: softmax over the selected experts (renormalize) or over all experts; the
  * unbiased sigmoid / sqrt(softplus) of the selected experts, divided by their sum when
  * renormalize (the sqrtsoftplus sum clamped at 1e-20); then times `scaling`.
  * experts in {64, 128, 256, 512}; 1 <= top_k <= 8. */
-EXF_API int exf_router_topk(const float* logits, int64_t tokens, int experts, int top_k,
-                            int scoring, const float* bias, int renormalize, float scaling,
-                            float* out_w, int32_t* out_ids, exf_stream_t stream);
+EXF_API int exf_router_topk(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                            int top_k, int scoring, const float* bias, int renormalize,
+                            float scaling, float* out_w, int32_t* out_ids, exf_stream_t stream);
 
 /* Hash routing of DeepSeek-V4's hash-MoE layers: replaces vLLM fused_topk_bias with
  * hash_indices_table = gate.tid2eid and input_tokens (exfold/deepseek_v4/vllm_patch.py:175-209).
  * The routes of token t are table[token_ids[t]][0..top_k) in table order, weights the unbiased
  * scores (scoring EXF_SIGMOID or EXF_SQRTSOFTPLUS; EXF_SOFTMAX is EXF_ERR_UNSUPPORTED) of those
  * experts, divided by their sum when renormalize (sqrtsoftplus: sum clamped at 1e-20), times
- * `scaling`.  logits [tokens][experts] fp32; token_ids [tokens] (id_dtype); table
+ * `scaling`.  logits [tokens][experts] of logit_dtype (as exf_router_topk); token_ids [tokens]
+ * (id_dtype); table
  * [table_rows][top_k] int32; outputs [tokens][top_k].  A token id outside the table gives ids -1
  * and weights 0; a table entry outside [0, experts) keeps its id with weight 0. */
-EXF_API int exf_router_hash(const float* logits, int64_t tokens, int experts, int top_k,
-                            int scoring, const void* token_ids, int id_dtype,
+EXF_API int exf_router_hash(const void* logits, int logit_dtype, int64_t tokens, int experts,
+                            int top_k, int scoring, const void* token_ids, int id_dtype,
                             const int32_t* table, int64_t table_rows, int renormalize,
                             float scaling, float* out_w, int32_t* out_ids, exf_stream_t stream);
 
 /* Router + prefill fold in one pass over the logits: the B200 form of the patched prefill router
  * (exfold/qwen3/vllm_patch.py:166-176 -> kernels.py:97-151; exfold/deepseek_v4/vllm_patch.py:
  * 262-284 -> exfold_kernels.cu:228-278).  `layers` independent layers are processed in one
- * launch: logits [layers][tokens][experts], bias [layers][experts], tables
+ * launch: logits [layers][tokens][experts] of logit_dtype (as exf_router_topk), bias
+ * [layers][experts], tables
  * [layers][experts][experts], outputs [layers][tokens][target_k].  conf_loss is used by
  * EXF_DSV4 with EXF_RENORM_SIMILARITY_BLEND only (may be NULL otherwise). */
-EXF_API int exf_router_fold_prefill(const float* logits, int64_t tokens, int layers, int experts,
-                                    int top_k, int scoring, const float* bias, int renormalize,
+EXF_API int exf_router_fold_prefill(const void* logits, int logit_dtype, int64_t tokens,
+                                    int layers, int experts, int top_k, int scoring,
+                                    const float* bias, int renormalize,
                                     float scaling, int target_k, int variant, int renorm_mode,
                                     const float* coeff, const float* sel_loss,
                                     const float* conf_loss, float* out_w, int32_t* out_ids,

@@ -28,7 +28,7 @@ def test_library_loads_and_exports_header_symbols():
         assert hasattr(lib, name), name
         assert name in L.SIGNATURES, f"{name} has no ctypes signature"
     assert set(L.SIGNATURES) == set(names)
-    assert lib.exf_abi_version() == 1
+    assert lib.exf_abi_version() == 2
 
 
 def test_capacity_matches_vllm_rule():
@@ -50,16 +50,24 @@ def last_error() -> str:
 
 def test_argument_validation_without_gpu():
     fake = ctypes.c_void_p(16)  # never dereferenced: validation fails first
-    rc = call("exf_router_topk", fake, 10, 96, 8, 0, None, 1, 1.0, fake, fake, None)
+    rc = call("exf_router_topk", fake, 0, 10, 96, 8, 0, None, 1, 1.0, fake, fake, None)
     assert rc == L.EXF_ERR_UNSUPPORTED and "experts" in last_error()
-    rc = call("exf_router_topk", fake, 10, 128, 9, 0, None, 1, 1.0, fake, fake, None)
+    rc = call("exf_router_topk", fake, 0, 10, 128, 9, 0, None, 1, 1.0, fake, fake, None)
     assert rc == L.EXF_ERR_INVALID and "top_k" in last_error()
-    rc = call("exf_router_topk", ctypes.c_void_p(20), 10, 128, 8, 0, None, 1, 1.0, fake, fake, None)
+    rc = call("exf_router_topk", ctypes.c_void_p(20), 0, 10, 128, 8, 0, None, 1, 1.0, fake, fake,
+              None)
     assert rc == L.EXF_ERR_INVALID and "aligned" in last_error()
-    rc = call("exf_router_fold_prefill", fake, 10, 1, 128, 8, 0, None, 1, 1.0, 9, 0, 0, fake, fake,
+    rc = call("exf_router_topk", fake, 5, 10, 128, 8, 0, None, 1, 1.0, fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "EXF_BF16" in last_error()
+    rc = call("exf_router_topk", ctypes.c_void_p(24), L.EXF_BF16, 10, 128, 8, 0, None, 1, 1.0,
+              fake, fake, None)
+    assert rc == L.EXF_ERR_INVALID and "aligned" in last_error()
+    rc = call("exf_router_fold_prefill", fake, 0, 10, 1, 128, 8, 0, None, 1, 1.0, 9, 0, 0, fake,
+              fake,
               None, fake, fake, None)
     assert rc == L.EXF_ERR_INVALID and "target_k" in last_error()
-    rc = call("exf_router_fold_prefill", fake, 10, 1, 128, 8, 0, None, 1, 1.0, 4, 0, 2, fake, fake,
+    rc = call("exf_router_fold_prefill", fake, 0, 10, 1, 128, 8, 0, None, 1, 1.0, 4, 0, 2, fake,
+              fake,
               None, fake, fake, None)
     assert rc == L.EXF_ERR_INVALID and "renorm_mode" in last_error()
     rc = call("exf_fold_prefill", fake, 7, fake, 0, 10, 8, 4, 128, 0, 0, fake, fake, None, fake,
@@ -102,7 +110,9 @@ def test_argument_validation_without_gpu():
 
 def test_empty_inputs_are_no_ops_without_gpu():
     # zero tokens returns before any CUDA call
-    assert call("exf_router_topk", None, 0, 128, 8, 0, None, 1, 1.0, None, None, None) == 0
+    assert call("exf_router_topk", None, 0, 0, 128, 8, 0, None, 1, 1.0, None, None, None) == 0
+    assert call("exf_router_topk", None, L.EXF_BF16, 0, 128, 8, 0, None, 1, 1.0, None, None,
+                None) == 0
     assert call("exf_fold_prefill", None, 0, None, 0, 0, 8, 4, 128, 0, 0, None, None, None, None,
                 None, None) == 0
 
