@@ -452,9 +452,13 @@ def config0(t: Timer, dev, peaks, steps) -> dict:
     ow = torch.empty((lay.tokens, KEEP), device=dev)
     oi = torch.empty((lay.tokens, KEEP), dtype=torch.int32, device=dev)
     ms = t.flushed(lambda: ops.router_fold_prefill(x, TOP_K, KEEP, c, l_, out=(ow, oi)), steps)
+    x16 = x.to(torch.bfloat16)
+    ms_16 = t.flushed(lambda: ops.router_fold_prefill(x16, TOP_K, KEEP, c, l_, out=(ow, oi)),
+                      steps)
     nbytes = lay.tokens * (128 * 4 + KEEP * 8) + 2 * 128 * 128 * 4
     return {"tokens": lay.tokens, "us": ms * 1e3, "tokens_per_s": lay.tokens / ms * 1e3,
-            "l2": "flushed between launches", "launches": 1, **_hbm(nbytes, ms, peaks)}
+            "l2": "flushed between launches", "launches": 1, **_hbm(nbytes, ms, peaks),
+            "bf16_logits_us": ms_16 * 1e3}
 
 
 def config1(t: Timer, dev, peaks, steps) -> dict:
@@ -530,11 +534,17 @@ def config2_fold(t: Timer, dev, peaks, steps, tokens=None):
                                 variant="dsv4", renorm_mode=2, conf_loss=cf, out=(ow, oi))
 
     ms_fold = t.flushed(fold, steps)
+    x16 = x_logits.to(torch.bfloat16)
+    ms_16 = t.flushed(lambda: ops.router_fold_prefill(
+        x16, 8, 3, c, l_, scoring="sigmoid", bias=b, variant="dsv4", renorm_mode=2,
+        conf_loss=cf, out=(ow, oi)), steps)
     fold()
     fbytes = lay.tokens * (256 * 4 + 3 * 8) + 3 * 256 * 256 * 4 + 256 * 4
+    fbytes16 = fbytes - lay.tokens * 256 * 2
     out = {"tokens": lay.tokens, "keep": 3, "renorm": "similarity_blend",
            "fold_us": ms_fold * 1e3, "fold_tokens_per_s": lay.tokens / ms_fold * 1e3,
-           "fold": _hbm(fbytes, ms_fold, peaks), "fold_l2": "flushed between launches"}
+           "fold": _hbm(fbytes, ms_fold, peaks), "fold_l2": "flushed between launches",
+           "fold_bf16_logits": {"us": ms_16 * 1e3, **_hbm(fbytes16, ms_16, peaks)}}
     return out, ow, oi
 
 

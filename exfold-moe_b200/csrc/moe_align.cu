@@ -184,12 +184,22 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const Alig
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
   const int E = p.experts;
+  // Column prefix of expert tid over the chunks.  The loads of kBatch chunks are issued before
+  // any of their stores: a load after a store to the same table cannot be hoisted above it, so a
+  // one-chunk-at-a-time loop would wait one L2 round trip per chunk.
+  constexpr int kBatch = 16;
   if (tid < E) {
     int run = 0;
-    for (int64_t b = 0; b < p.chunks; ++b) {
-      const int c = p.table[b * E + tid];
-      p.table[b * E + tid] = run;  // routes of expert tid in chunks before b
-      run += c;
+    for (int64_t b0 = 0; b0 < p.chunks; b0 += kBatch) {
+      int c[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) c[j] = b0 + j < p.chunks ? p.table[(b0 + j) * E + tid] : 0;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (b0 + j < p.chunks) {
+          p.table[(b0 + j) * E + tid] = run;  // routes of expert tid in chunks before b0 + j
+          run += c[j];
+        }
     }
     sm.count[tid] = run;
   }
@@ -197,7 +207,14 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const Alig
   scan_and_fill(p, sm);
   if (tid < E) {
     const int o = sm.off[tid];
-    for (int64_t b = 0; b < p.chunks; ++b) p.table[b * E + tid] += o;
+    for (int64_t b0 = 0; b0 < p.chunks; b0 += kBatch) {
+      int c[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) c[j] = b0 + j < p.chunks ? p.table[(b0 + j) * E + tid] : 0;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (b0 + j < p.chunks) p.table[(b0 + j) * E + tid] = c[j] + o;
+    }
   }
 }
 

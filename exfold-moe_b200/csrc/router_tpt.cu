@@ -5,12 +5,15 @@
 //   * The logits stream through a ring of 10 tile slots (32 tokens x 512 B each) per CTA, filled
 //     by bulk copies (cp.async.bulk, mbarrier completion) and shared by 10 warps (168
 //     registers each; 10 rather than 8 warps: 2.8 instead of 3.5 tiles per warp and launch at
-//     131072 tokens, 23.1 instead of 24.6 us per launch): a warp takes
+//     131072 tokens, 23.1 instead of 24.6 us per launch; 16-bit logits: 20 slots of 8 KB shared
+//     by 14 warps): a warp takes
 //     the next tile of the layer, ranks it, and refills the slot with the tile 10 places ahead
 //     as soon as its selection has read it, publishing the tile index so that the slot's next
 //     reader knows which barrier phase to wait for.  Lane t owns token t of the tile and reads
 //     its row in the chunk order i ^ (t & 7): rows are 512 B apart, so the 8 lanes of each
-//     quarter-warp hit 8 different 16-byte bank quads and the reads are conflict-free.
+//     quarter-warp hit 8 different 16-byte bank quads and the reads are conflict-free.  bf16 /
+//     fp16 logits: 8 KB tiles in twice the slots, 8-byte chunks in the order i ^ (t & 15), and
+//     exact group-maximum keys (below), so ties need no fallback.
 //   * Selection keys are IEEE totalOrder keys of the logits.  The 32 groups of 4 consecutive
 //     columns give 32 group maxima; their keys, with the low 5 bits replaced by the group's slot,
 //     go through a sorting network (4 x 19-comparator sorts, 3 merges) whose top 8 name the 8
@@ -19,7 +22,9 @@
 //     column asc)), and every other element of those groups that reaches the 8th maximum is
 //     inserted.  When the 9th largest maximum (the largest value the merges drop) is below the
 //     8th in its truncated key and the 8th maximum is positive, this is the exact top 8 (every
-//     element that reaches it lies in those groups; no zeros, so -0 and +0 cannot tie).  Other
+//     element that reaches it lies in those groups; no zeros, so -0 and +0 cannot tie).  For
+//     16-bit logits the truncation loses nothing and equal keys sort by group, so only the sign
+//     of the 8th maximum and NaN rows decide.  Other
 //     tokens (a group outside the 8 close to the 8th maximum, zeros among the candidates, NaN)
 //     insert every element of every group that reaches the truncated bound instead (every
 //     element, for a row with a NaN): exact, slower.
@@ -44,14 +49,18 @@ using namespace tile;
 
 constexpr int kE = 128;
 constexpr int kK = 8;
-#ifndef EXF_TPT_WARPS
-#define EXF_TPT_WARPS 10
-#endif
 #ifndef EXF_TPT_SLOTS
 #define EXF_TPT_SLOTS 10
 #endif
-constexpr int kWarps = EXF_TPT_WARPS;    // warps per CTA, each ranking one tile at a time
 constexpr int kRows = 32;                // tokens per tile: one per lane
+// Warps per CTA, each ranking one tile at a time.  A warp's tile latency bounds the kernel, so
+// more warps help until the register file (168 registers a thread) runs out: 10 for fp32 logits
+// (12-16 measured slower per launch: they share 10 slots), 14 for 16-bit logits with their
+// 20 slots (21.7 us per 131072-token launch against 23.6 us with 10 warps).
+template <typename LT>
+constexpr int tpt_warps() {
+  return sizeof(LT) == 4 ? 10 : 14;
+}
 
 // Tile slots per CTA (a ring shared by its warps): 16 KB tiles of fp32 logits, 8 KB of bf16 /
 // fp16 logits, so the 16-bit ring has twice the slots in the same shared memory.
@@ -101,7 +110,7 @@ __device__ __noinline__ void exact_top8(const LT* rowp, int swz, uint32_t lb, ui
 }
 
 template <int FOLD, int P, typename LT>
-__global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const RouterParams p) {
+__global__ void __launch_bounds__(tpt_warps<LT>() * 32, 1) router_tpt_kernel(const RouterParams p) {
   extern __shared__ uint8_t tpt_raw[];
   using Smem = TptSmem<LT>;
   constexpr int kSlots = Smem::kSlots;
@@ -212,19 +221,23 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
 
       // ======== phase 1: the selection, the only part that reads the tile =====================
       if (ok) {
-        // ---- group maxima (slot u holds columns 4 (u ^ swz) .. + 3) ---------------------------
+        // ---- group maxima (step u reads group u ^ swz: columns 4 (u ^ swz) .. + 3) ------------
         // A float maximum keyed once equals the key maximum except that -0 may stand for +0
         // (harmless: zeros never reach the fast path's theta, and the exact path merges them);
         // a NaN makes the group's key all ones, which the exact path below takes over.  The key
-        // keeps its high 27 bits; the low 5 name the slot.
+        // keeps its high 27 bits; the low 5 hold 31 - u (fp32: a constant per step) or, for
+        // 16-bit logits, 31 - group, so that equal keys sort by ascending group, i.e. ascending
+        // column.
+        constexpr bool kExactKeys = sizeof(LT) == 2;
         uint32_t pk[32];
 #pragma unroll
         for (int s = 0; s < 4; ++s)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 v = load_logits4(rowp + 4 * ((8 * s + i) ^ swz));
+            const uint32_t grp = static_cast<uint32_t>((8 * s + i) ^ swz);
+            const float4 v = load_logits4(rowp + 4 * grp);
             const uint32_t g = order_key(fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
-            pk[8 * s + i] = (g & ~31u) | (31u - (8 * s + i));
+            pk[8 * s + i] = (g & ~31u) | (31u - (kExactKeys ? grp : 8 * s + i));
           }
         sort8<uint32_t, cx32>(pk);
         sort8<uint32_t, cx32>(pk + 8);
@@ -240,8 +253,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
         int cb[kK], emax[kK];
 #pragma unroll
         for (int i = 0; i < kK; ++i) {
-          const uint32_t u = 31u - (pk[i] & 31u);
-          cb[i] = 4 * static_cast<int>(u ^ static_cast<uint32_t>(swz));
+          const uint32_t slot = 31u - (pk[i] & 31u);
+          cb[i] = 4 * static_cast<int>(kExactKeys ? slot : slot ^ static_cast<uint32_t>(swz));
           const float4 v = load_logits4(rowp + cb[i]);
           ek[i][0] = order_key(v.x);
           ek[i][1] = order_key(v.y);
@@ -251,15 +264,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
           emax[i] = ek[i][0] == m ? 0 : (ek[i][1] == m ? 1 : (ek[i][2] == m ? 2 : 3));
           T[i] = pack(m, cb[i] + emax[i]);
         }
-        // distinct truncated keys: the exact maxima are already in descending order
+        // A 16-bit logit converted to fp32 has its low 16 bits all zeros (its key all zeros or
+        // all ones there), so for 16-bit logits the truncated keys are exact: the named groups'
+        // maxima are in (key desc, column asc) order, and an element of any other group either
+        // is below the 8th maximum or equals it at a higher column, so it is not in the top 8.
+        // fp32 keys lose their low 5 bits: the order holds when the truncated keys differ, and
+        // the other groups are excluded when the 9th truncated maximum is below the 8th.
         bool distinct = true;
+        if (!kExactKeys) {
 #pragma unroll
-        for (int i = 0; i + 1 < kK; ++i) distinct = distinct && (pk[i] >> 5) != (pk[i + 1] >> 5);
+          for (int i = 0; i + 1 < kK; ++i)
+            distinct = distinct && (pk[i] >> 5) != (pk[i + 1] >> 5);
+        }
         if (!distinct) sort8<uint64_t, cx64>(T);
         const uint32_t theta = static_cast<uint32_t>(T[kK - 1] >> 32);
-        // every other group's truncated maximum below the 8th: each element that reaches theta
-        // lies in the 8 named groups
-        const bool apart = (p9 >> 5) < (pk[kK - 1] >> 5);
+        const bool apart = kExactKeys || (p9 >> 5) < (pk[kK - 1] >> 5);
         const bool nan_row = pk[0] >= 0xFFFFFFE0u;
         const bool fast = apart && theta > kKeyPosZero && !nan_row;
 
@@ -269,11 +288,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
           uint32_t xm = 0, slo = 0, shi = 0;
 #pragma unroll
           for (int i = 0; i < kK; ++i) {
-            const uint32_t u = 31u - (pk[i] & 31u);
+            const uint32_t grp = static_cast<uint32_t>(cb[i]) >> 2;
             if (i < 6)
-              slo |= u << (5 * i);
+              slo |= grp << (5 * i);
             else
-              shi |= u << (5 * (i - 6));
+              shi |= grp << (5 * (i - 6));
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               xm |= (e != emax[i] && ek[i][e] >= theta ? 1u : 0u) << (4 * i + e);
@@ -282,8 +301,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_tpt_kernel(const Router
             const int site = __ffs(xm) - 1;
             xm &= xm - 1;
             const int i = site >> 2;
-            const uint32_t u = (i < 6 ? slo >> (5 * i) : shi >> (5 * (i - 6))) & 31u;
-            const int col = 4 * static_cast<int>(u ^ static_cast<uint32_t>(swz)) + (site & 3);
+            const uint32_t grp = (i < 6 ? slo >> (5 * i) : shi >> (5 * (i - 6))) & 31u;
+            const int col = 4 * static_cast<int>(grp) + (site & 3);
             insert8(T, pack(order_key(logit_f32<LT>(rowp[col])), col));
           }
         } else if (valid) {
@@ -443,7 +462,7 @@ cudaError_t launch_tpt_l(const RouterParams& p, cudaStream_t stream) {
   if (blocks < 1) blocks = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-  cfg.blockDim = dim3(kWarps * 32);
+  cfg.blockDim = dim3(tpt_warps<LT>() * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
