@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_scan_kernel(const Alig
   // Column prefix of expert tid over the chunks.  The loads of kBatch chunks are issued before
   // any of their stores: a load after a store to the same table cannot be hoisted above it, so a
   // one-chunk-at-a-time loop would wait one L2 round trip per chunk.
-  constexpr int kBatch = 16;
+  constexpr int kBatch = 32;
   if (tid < E) {
     int run = 0;
     for (int64_t b0 = 0; b0 < p.chunks; b0 += kBatch) {
