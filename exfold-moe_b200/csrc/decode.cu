@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
 // read-only path.
 template <typename WT, typename IT, bool ALIGN>
 __device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm) {
-  constexpr int kBlock = 128;
+  const int kBlock = p.align_block > 0 ? p.align_block : 128;
   const int E = p.experts;
   const int K = p.top_k;
   const int R = static_cast<int>(p.routes);

@@ -88,9 +88,10 @@ struct DecodeParams {
   int top_k;
   float* gemm_w;            // [routes] weights for the expert layer (merged in slot order)
   int32_t* gemm_ids;        // [routes] expert of each route; -1 for a merged or invalid route
-  int32_t* sorted_ids;      // moe_align outputs over gemm_ids, 128-row blocks
+  int32_t* sorted_ids;      // moe_align outputs over gemm_ids, align_block-route blocks
   int32_t* block_experts;
   int32_t* num_post_pad;
+  int align_block;          // moe_align block size of the fused path (0: 128)
   // kImportanceExchanged only: this process's mapping of every rank's exchange buffer
   int world;
   int rank;

@@ -1,6 +1,7 @@
 // Grouped SwiGLU expert GEMMs on the 5th-generation tensor cores (sm_100a: tcgen05 + TMA).
 //
-// After moe_align, routes are grouped by expert and padded to 128-row blocks.  Per MoE layer:
+// After moe_align, routes are grouped by expert and padded to blocks (128 routes at prefill, 64 at
+// decode).  Per MoE layer:
 //   gather : xs[m] = x[token(sorted_ids[m])]                      (bf16 rows of real routes)
 //   GEMM-1 : act[m, n] = silu(xs[m] . W1[e, n]) * (xs[m] . W3[e, n]) for n in a 128-wide tile;
 //            gate and up rows of W13[e] are stacked into one N = 256 MMA so both accumulators
@@ -8,15 +9,17 @@
 //   GEMM-2 : out[route, h] = w_route * (act[m] . W2[e, h])         (N = 256 tile of H)
 //   combine: y[t, h] = sum over the token's routes of out[route, h] (fixed order: deterministic)
 //
-// Both GEMMs share one mainloop in a persistent kernel: one CTA per SM walks 128 x BN output
-// tiles (one expert each; BN = 256, or 128 when the experts hold few routes, as at decode);
-// warp 0 streams 128 x 64 A and BN x 64 B bf16 tiles with TMA (128-byte swizzle) through a
-// 4-stage (6 at BN = 128) mbarrier ring that runs on across tiles; one elected
+// Prefill (expert_gemm_kernel): routes on the M side.  Both GEMMs share one mainloop in a
+// persistent kernel: one CTA per SM walks 128 x 256 output tiles (one expert each); warp 0
+// streams 128 x 64 A and 256 x 64 B bf16 tiles with TMA (128-byte swizzle) through a 4-stage
+// mbarrier ring that runs on across tiles; one elected
 // thread of warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16, fp32 accumulation in TMEM) and
 // releases each stage with tcgen05.commit; warps 2-5 read the accumulator with tcgen05.ld and run
 // the epilogue.  Two TMEM accumulators (all 512 columns) let the epilogue of one tile overlap
 // the mainloop of the next.  The N tiles of one M block run side by side on neighbouring CTAs,
 // so A tiles and the expert's weight tiles are reused from L2.
+// Decode (expert_gemm_t_kernel, experts holding 64 routes or fewer on average): weight rows on
+// the M side, blocks of 64 routes on the N side (see the comment above that kernel).
 // Every mbarrier wait is bounded: on time-out the CTA records an error in *status, skips the
 // rest of its work, still frees its TMEM and returns.
 #include <cuda.h>
@@ -38,9 +41,8 @@ constexpr int kATileBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kGemmThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTmemCols = 512;       // two accumulators of up to 256 fp32 columns
 
-// The MMA N tile: 256 for prefill; 128 when experts hold few routes (decode), which doubles the
-// tiles over the same weight bytes (2.6 -> 5.2 tiles per CTA at the Qwen3 decode shape, so the
-// last round idles fewer SMs) with 6 stages of 32 KB instead of 4 of 48 KB.
+// The MMA N tile of the prefill kernel: 256 (4 stages of 48 KB); 128 (6 stages of 32 KB) is
+// kept as a configuration.
 template <int BN>
 struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : 6;
@@ -258,6 +260,222 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0 && sm.failed && p.status) atomicExch(p.status, 1);
 }
 
+// ---- decode: routes on the N side -------------------------------------------------------------
+// At decode an expert holds a few routes, so a 128-row block of routes is mostly padding, and the
+// MMA work of that padding, not the weight stream, bounds the layer (with the weight loads taken
+// out, the Qwen3 decode layer took 169 us instead of 160).  Here a tile is 128 weight rows of one
+// expert (the M side, all real) times a block of BT = 64 of its routes (the N side; the moe_align
+// block size of this path), so the MMA work follows the real routes and 80 % of each GEMM-1
+// pipeline stage is weights.
+//   GEMM-1: Dg[f][r] = W1[e][f] . xs[r] and Du[f][r] = W3[e][f] . xs[r] in two accumulators; the
+//           epilogue writes act[r][f] = silu(Dg) * Du for the block's real routes;
+//   GEMM-2: D[h][r] = W2[e][h] . act[r]; the epilogue writes out[route][h] = w_route * D.
+// Tiles t = block * feature_tiles + feature_tile: the CTAs running at one time stream neighbouring
+// row slabs of a few experts' weights (block-major measured 4-12 % faster than feature-tile-major,
+// which spreads them over as many experts as CTAs).  Roles, pipeline, TMEM double buffering and
+// bounded waits as in expert_gemm_kernel.
+template <int KIND, int BT>
+struct TCfg {
+  static constexpr int kWTile = 128 * kBK * 2;   // 16 KB: 128 weight rows x 64 K
+  static constexpr int kTTile = BT * kBK * 2;    // BT route rows x 64 K
+  static constexpr int kWTiles = KIND == kGemmSwiGLU ? 2 : 1;   // gate and up, or W2
+  static constexpr int kStageBytes = kWTiles * kWTile + kTTile;
+  static constexpr int kStages = (200 * 1024) / kStageBytes;
+  static constexpr int kAccCols = kWTiles * BT;  // TMEM columns of one tile's accumulators
+  static constexpr int kTmemCols = 2 * kAccCols; // two tiles in flight: 64 .. 256, a power of 2
+  static constexpr uint32_t kIdesc = idesc_f16(128, BT, true);  // bf16, M = 128, N = BT
+};
+
+template <int KIND, int BT>
+struct TSmem {
+  alignas(1024) uint8_t tiles[TCfg<KIND, BT>::kStages][TCfg<KIND, BT>::kStageBytes];
+  alignas(8) uint64_t full[TCfg<KIND, BT>::kStages];
+  alignas(8) uint64_t empty[TCfg<KIND, BT>::kStages];
+  alignas(8) uint64_t acc_full[2];
+  alignas(8) uint64_t acc_empty[2];
+  alignas(8) uint64_t drain;
+  uint32_t tmem_base;
+  int failed;
+};
+template <int KIND, int BT>
+constexpr size_t tgemm_smem_bytes() { return sizeof(TSmem<KIND, BT>) + 1024; }
+static_assert(tgemm_smem_bytes<kGemmSwiGLU, 64>() <= 232448, "decode GEMM shared memory");
+static_assert(tgemm_smem_bytes<kGemmDown, 64>() <= 232448, "decode GEMM shared memory");
+
+template <int KIND, int BT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    expert_gemm_t_kernel(const __grid_constant__ CUtensorMap map_w,
+                         const __grid_constant__ CUtensorMap map_t, const ExpertGemmParams p) {
+  using C = TCfg<KIND, BT>;
+  constexpr int kStages = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  TSmem<KIND, BT>& sm = *reinterpret_cast<TSmem<KIND, BT>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&sm.drain, 1);
+    sm.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, C::kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  const int post = *p.num_post_pad;
+  const int m_used = (post + BT - 1) / BT < p.m_blocks ? (post + BT - 1) / BT : p.m_blocks;
+  const int ntiles = m_used * p.n_tiles;
+  auto tile_expert = [&](int t, int& blk, int& ft) {
+    blk = t / p.n_tiles;
+    ft = t - blk * p.n_tiles;
+    const int e = p.expert_ids[blk];
+    return (e >= 0 && e < p.experts) ? e : -1;
+  };
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* failed = &sm.failed;
+  const int kblocks = p.k / kBK;
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int blk, ft;
+        const int expert = tile_expert(t, blk, ft);
+        if (expert < 0) continue;
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kStages;
+          ok = mbar_wait(&sm.empty[s], ((g / kStages) & 1) ^ 1, failed);
+          if (!ok) break;
+          uint8_t* st = sm.tiles[s];
+          mbar_expect_tx(&sm.full[s], C::kStageBytes);
+          if (KIND == kGemmSwiGLU) {
+            // gate rows [f0, f0 + 128) and up rows [I + f0, I + f0 + 128) of W13[expert]
+            const int row0 = expert * 2 * p.n_total + ft * 128;
+            tma_load_2d(st, &map_w, &sm.full[s], kb * kBK, row0);
+            tma_load_2d(st + C::kWTile, &map_w, &sm.full[s], kb * kBK, row0 + p.n_total);
+          } else {
+            tma_load_2d(st, &map_w, &sm.full[s], kb * kBK, expert * p.n_total + ft * 128);
+          }
+          tma_load_2d(st + C::kWTiles * C::kWTile, &map_t, &sm.full[s], kb * kBK, blk * BT);
+        }
+      }
+      for (uint32_t j = g > kStages ? g - kStages : 0; j < g; ++j)
+        mbar_wait_drain(&sm.full[j % kStages], (j / kStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: tile i accumulates into TMEM columns [kAccCols (i & 1), +kAccCols)
+    if (lane == 0) {
+      uint32_t g = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int blk, ft;
+        if (tile_expert(t, blk, ft) < 0) continue;
+        const int b = i & 1;
+        ok = mbar_wait(&sm.acc_empty[b], ((i >> 1) & 1) ^ 1, failed);
+        if (!ok) break;
+        fence_after_sync();
+        const uint32_t acc = tmem + static_cast<uint32_t>(b * C::kAccCols);
+        for (int kb = 0; kb < kblocks; ++kb, ++g) {
+          const int s = g % kStages;
+          ok = mbar_wait(&sm.full[s], (g / kStages) & 1, failed);
+          if (!ok) break;
+          fence_after_sync();
+          const uint32_t w_base = smem_addr(sm.tiles[s]);
+          const uint32_t t_base = w_base + C::kWTiles * C::kWTile;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint32_t on = (kb > 0 || k > 0) ? 1u : 0u;
+            mma_kind_f16(acc, smem_desc(w_base + k * 32), smem_desc(t_base + k * 32), C::kIdesc,
+                         on);
+            if (KIND == kGemmSwiGLU)
+              mma_kind_f16(acc + BT, smem_desc(w_base + C::kWTile + k * 32),
+                           smem_desc(t_base + k * 32), C::kIdesc, on);
+          }
+          mma_commit(&sm.empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&sm.acc_full[b]);
+        ++i;
+      }
+      mma_commit(&sm.drain);
+      mbar_wait_drain(&sm.drain, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2-5 own TMEM lanes 32 (warp % 4) .. +31 = 32 weight rows (features);
+    // columns are the block's routes.  Lane j fetches route j of each 32-route chunk and shares it.
+    const int q = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      int blk, ft;
+      if (tile_expert(t, blk, ft) < 0) continue;
+      const int b = i & 1;
+      const bool ok = mbar_wait(&sm.acc_full[b], (i >> 1) & 1, failed);
+      fence_after_sync();
+      if (!ok || *failed) break;
+      const int feat = ft * 128 + q * 32 + lane;
+      const uint32_t taddr =
+          tmem + static_cast<uint32_t>(b * C::kAccCols) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BT; c += 32) {
+        const int row_l = blk * BT + c + lane;  // this lane's route row of the chunk
+        const int route_l = p.sorted_ids[row_l];
+        const bool real_l = route_l < p.numel;
+        if (KIND == kGemmSwiGLU) {
+          float gt[32], up[32];
+          tmem_load32(taddr + c, gt);
+          tmem_load32(taddr + BT + c, up);
+          __nv_bfloat16* dst = p.act + (int64_t)(blk * BT + c) * p.n_total + feat;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const bool real = __shfl_sync(0xffffffffu, real_l, j);
+            if (real)
+              dst[(int64_t)j * p.n_total] =
+                  __float2bfloat16_rn(gt[j] / (1.0f + __expf(-gt[j])) * up[j]);
+          }
+        } else {
+          const float w_l = real_l ? p.route_w[route_l] : 0.0f;
+          float v[32];
+          tmem_load32(taddr + c, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int route = __shfl_sync(0xffffffffu, route_l, j);
+            const float wr = __shfl_sync(0xffffffffu, w_l, j);
+            if (route < p.numel)
+              p.out[(int64_t)route * p.hidden + feat] = __float2bfloat16_rn(v[j] * wr);
+          }
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+      ++i;
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after_sync();
+    tmem_free(tmem, C::kTmemCols);
+  }
+  if (threadIdx.x == 0 && sm.failed && p.status) atomicExch(p.status, 1);
+}
+
 // ---- gather and combine ---------------------------------------------------------------------
 // xs[m] = x[sorted_ids[m] / top_k] for the real routes of the used rows (16-byte vectors).
 // Padding rows keep whatever the workspace holds: the GEMM rows are independent, GEMM-1's
@@ -328,15 +546,17 @@ static cudaError_t allow_gemm_smem() {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   if (done[dev]) return cudaSuccess;
-  const int s256 = (int)gemm_smem_bytes<256>(), s128 = (int)gemm_smem_bytes<128>();
-  if ((e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 256>,
+  const int s256 = (int)gemm_smem_bytes<256>();
+  if ((e = cudaFuncSetAttribute(expert_gemm_t_kernel<kGemmSwiGLU, 64>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)tgemm_smem_bytes<kGemmSwiGLU, 64>())) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(expert_gemm_t_kernel<kGemmDown, 64>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)tgemm_smem_bytes<kGemmDown, 64>())) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 256>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess ||
       (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown, 256>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 128>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, s128)) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown, 128>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, s128)) != cudaSuccess)
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess)
     return e;
   done[dev] = true;
   return cudaSuccess;
@@ -391,7 +611,7 @@ MoeWorkspace moe_workspace(int64_t tokens, int top_k, int experts, int hidden, i
   };
   w.capacity = cap;
   w.sorted_ids = reinterpret_cast<int32_t*>(take(cap * 4));
-  w.expert_ids = reinterpret_cast<int32_t*>(take((cap / kBM) * 4));
+  w.expert_ids = reinterpret_cast<int32_t*>(take((cap / 64) * 4));  // blocks of 64 routes or more
   w.num_post_pad = reinterpret_cast<int32_t*>(take(4));
   w.align_bytes = align_workspace_bytes(numel, experts);
   w.align_ws = take(w.align_bytes > 0 ? w.align_bytes : 4);
@@ -440,7 +660,56 @@ static cudaError_t launch_gemms(const MoeArgs& a, const MoeWorkspace& w, cudaStr
                     s, ma, mb, p);
 }
 
-// Steps 2-5 of launch_moe_experts, from routes already aligned into w.
+// GEMM-1 and GEMM-2 with the routes on the N side (decode; see expert_gemm_t_kernel), over routes
+// aligned into blocks of BT.
+template <int BT>
+static cudaError_t launch_gemms_t(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+  const int64_t cap = w.capacity;
+  CUtensorMap mw, mt;
+  if (!make_map(&mw, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, 128) ||
+      !make_map(&mt, w.xs, cap, a.hidden, BT))
+    return cudaErrorInvalidValue;
+  ExpertGemmParams p{};
+  p.num_post_pad = w.num_post_pad;
+  p.expert_ids = w.expert_ids;
+  p.sorted_ids = w.sorted_ids;
+  p.experts = a.experts;
+  p.numel = (int)(a.tokens * a.top_k);
+  p.hidden = a.hidden;
+  p.status = a.status;
+  p.k = a.hidden;
+  p.n_total = a.inter;
+  p.act = w.act;
+  p.m_blocks = (int)(cap / BT);
+  p.n_tiles = a.inter / 128;
+  const int sms = sm_count();
+  const unsigned grid = sms > 0 ? (unsigned)sms : 1u;
+  cudaError_t e = launch_pdl(expert_gemm_t_kernel<kGemmSwiGLU, BT>, grid, kGemmThreads,
+                             tgemm_smem_bytes<kGemmSwiGLU, BT>(), s, mw, mt, p);
+  if (e != cudaSuccess) return e;
+  if (!make_map(&mw, a.w2, (uint64_t)a.experts * a.hidden, a.inter, 128) ||
+      !make_map(&mt, w.act, cap, a.inter, BT))
+    return cudaErrorInvalidValue;
+  p.k = a.inter;
+  p.n_total = a.hidden;
+  p.route_w = a.topk_w;
+  p.out = w.out;
+  p.n_tiles = a.hidden / 128;
+  return launch_pdl(expert_gemm_t_kernel<kGemmDown, BT>, grid, kGemmThreads,
+                    tgemm_smem_bytes<kGemmDown, BT>(), s, mw, mt, p);
+}
+
+// The moe_align block size, which also picks the GEMM kernels: 128-row blocks of routes on the M
+// side (prefill); when the experts hold 64 routes or fewer on average (decode), blocks of 64
+// routes on the N side.  (Blocks of 32 measured at most 2 % faster on a few decode shapes and
+// 43 % slower at 512 tokens x top-8 over 64 experts: an expert's two blocks read its weights
+// twice.)
+constexpr int kDecodeBlock = 64;
+static int gemm_block(int64_t numel, int experts) {
+  return numel > (int64_t)experts * 64 ? kBM : kDecodeBlock;
+}
+
+// Steps 2-5 of launch_moe_experts, from routes already aligned into w (blocks of gemm_block).
 static cudaError_t launch_moe_compute(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
   const int64_t numel = a.tokens * a.top_k;
   const int64_t cap = w.capacity;
@@ -458,9 +727,9 @@ static cudaError_t launch_moe_compute(const MoeArgs& a, const MoeWorkspace& w, c
                    w.xs);
     if (e != cudaSuccess) return e;
   }
-  // 3-4. GEMM-1 + SwiGLU, GEMM-2 (N tile 128 when the experts hold 64 routes or fewer on
-  // average, as at decode; 256 otherwise)
-  e = numel <= (int64_t)a.experts * 64 ? launch_gemms<128>(a, w, s) : launch_gemms<256>(a, w, s);
+  // 3-4. GEMM-1 + SwiGLU, GEMM-2
+  e = gemm_block(numel, a.experts) == kDecodeBlock ? launch_gemms_t<kDecodeBlock>(a, w, s)
+                                                   : launch_gemms<256>(a, w, s);
   if (e != cudaSuccess) return e;
   // 5. combine the routes of each token
   {
@@ -475,8 +744,9 @@ static cudaError_t launch_moe_compute(const MoeArgs& a, const MoeWorkspace& w, c
 }
 
 cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
-  // 1. moe_align with the GEMM's 128-row blocks
-  AlignParams ap{a.topk_ids, a.tokens * a.top_k, a.experts, kBM, w.capacity, w.sorted_ids,
+  // 1. moe_align with the GEMM's blocks
+  AlignParams ap{a.topk_ids, a.tokens * a.top_k, a.experts,
+                 gemm_block(a.tokens * a.top_k, a.experts), w.capacity, w.sorted_ids,
                  w.expert_ids, w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
   const cudaError_t e = launch_align(0 /*int32*/, ap, s);
   return e != cudaSuccess ? e : launch_moe_compute(a, w, s);
@@ -498,6 +768,7 @@ cudaError_t launch_decode_moe_experts(DecodeParams d, const MoeArgs& a, void* wo
   d.sorted_ids = w.sorted_ids;
   d.block_experts = w.expert_ids;
   d.num_post_pad = w.num_post_pad;
+  d.align_block = gemm_block(a.tokens * a.top_k, a.experts);
   // 1. decode and moe_align in one launch (the merged routes)
   cudaError_t e = launch_decode_align(d, s);
   if (e != cudaSuccess) return e;
