@@ -363,20 +363,27 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       const int64_t tok_a = (tile0 + j) * kRows, tok_b = tok_a + kRows;
       const int ra = tok_a + r < tokens ? r : 0;
       const int rb = has_b && tok_b + r < tokens ? r : 0;
-      uint32_t pka[kK], pkb[kK] = {}, p9a = 0, p9b = 0, p10a = 0, p10b = 0;
-      bool ok = group_maxima(ks + j, ra, pka, p9a, p10a);
-      if (has_b) ok = group_maxima(ks + j + 1, rb, pkb, p9b, p10b) && ok;
-      // this lane's token from here on: r of A (h = 0) or r of B (h = 1); a lane without a token
-      // ranks A's (in bounds, discarded)
+      // this lane's token from phase 2 on: r of A (h = 0) or r of B (h = 1); a lane without a
+      // token ranks A's (in bounds, discarded)
       const bool use_b = h && has_b;
+      // Tiles A and B in a loop that is not unrolled (one copy of the group-maxima code: the
+      // kernel's instruction fetch was a top stall); each lane keeps its own tile's result.
+      uint32_t pk[kK] = {}, p9 = 0, p10 = 0;
+      bool ok = true;
+#pragma unroll 1
+      for (int which = 0; which < (has_b ? 2 : 1); ++which) {
+        uint32_t tk[kK], t9 = 0, t10 = 0;
+        ok = group_maxima(ks + j + which, which ? rb : ra, tk, t9, t10) && ok;
+        if (which == (use_b ? 1 : 0)) {
+#pragma unroll
+          for (int q = 0; q < kK; ++q) pk[q] = tk[q];
+          p9 = t9;
+          p10 = t10;
+        }
+      }
       const bool valid = use_b ? tok_b + r < tokens : (h == 0 && tok_a + r < tokens);
       const int64_t orow = l * tokens + (use_b ? tok_b : tok_a) + r;
       const LT* grow = logits + (l * tokens + (use_b ? tok_b + rb : tok_a + ra)) * kE;
-      uint32_t pk[kK];
-#pragma unroll
-      for (int q = 0; q < kK; ++q) pk[q] = use_b ? pkb[q] : pka[q];
-      const uint32_t p9 = use_b ? p9b : p9a;
-      const uint32_t p10 = use_b ? p10b : p10a;
 
       if (!ok) {
         if (valid) {
