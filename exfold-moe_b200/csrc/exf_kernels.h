@@ -142,6 +142,12 @@ cudaError_t launch_static_remap(int w_dtype, int id_dtype, void* w, void* ids, i
                                 int experts, const int32_t* target, const float* scale,
                                 cudaStream_t s);
 cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s);
+// moe_align of int32 ids fused with the gather of token rows for the expert layer:
+// xs[slot] = x[sorted_ids[slot] / top_k] (bf16 rows of `hidden`) for every placed route; at most
+// align_gather_max_numel() routes.  zero[0, zero_n) is set to 0 as well (may be null / 0).
+int64_t align_gather_max_numel();
+cudaError_t launch_align_gather(const AlignParams& p, const void* x, int top_k, int hidden,
+                                void* xs, int32_t* zero, int zero_n, cudaStream_t s);
 cudaError_t launch_calib_update(int out_dtype, int id_dtype, const void* out, const void* ids,
                                 int64_t tokens, int K, int H, int E, double* dot, double* tsq,
                                 double* ssq, double* nsum, double* ncnt, cudaStream_t s);

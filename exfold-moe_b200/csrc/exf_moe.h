@@ -52,6 +52,10 @@ struct MoeWorkspace {
   __nv_bfloat16* xs;
   __nv_bfloat16* act;
   __nv_bfloat16* out;
+  // the decode expert layer kernel's counters: [0] the next tile to hand out, [1 + b] the GEMM-1
+  // tiles of route block b finished (zeroed by the gather before each layer)
+  int32_t* layer_sync;
+  int layer_sync_ints;
   int64_t bytes;
 };
 

@@ -2,7 +2,8 @@
 // GEMM block size, name each block's expert.  Routes of one expert keep ascending flat order
 // (a stable counting sort), so the permutation is deterministic.
 //
-// numel <= kAlignSmall: one CTA does count, scan and stable scatter in shared memory.
+// numel <= kAlignSmall: one CTA does count, scan and stable scatter in shared memory (or, for
+// the expert layer, every CTA counts and each places and gathers a slice of the routes).
 // Larger: count (one CTA per 2048-route chunk, shared-memory histogram) -> scan (one CTA:
 // column prefix over chunks, padded exclusive scan over experts, padding and block->expert
 // fill) -> stable scatter (one CTA per chunk).  The [chunks][experts] int32 table lives in the
@@ -37,8 +38,8 @@ __device__ __forceinline__ int expert_of(const IT* ids, int64_t r, int64_t end, 
 
 // One round of the stable scatter: route r (expert e, -1 for none) of the CTA's 512 consecutive
 // routes goes to base[e] + (routes of expert e before it in the round); base advances.
-__device__ __forceinline__ void scatter_round(int64_t r, int e, int E, AlignSmem& sm,
-                                              int32_t* sorted_ids) {
+__device__ __forceinline__ int scatter_round(int64_t r, int e, int E, AlignSmem& sm,
+                                             int32_t* sorted_ids) {
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -49,10 +50,12 @@ __device__ __forceinline__ void scatter_round(int64_t r, int e, int E, AlignSmem
   const int lane_rank = __popc(m & lt);
   if (e >= 0 && lane_rank == 0) sm.wcnt[warp][e] = __popc(m);
   __syncthreads();
+  int slot = -1;
   if (e >= 0) {
     int prefix = 0;
     for (int w = 0; w < warp; ++w) prefix += sm.wcnt[w][e];
-    sorted_ids[sm.base[e] + prefix + lane_rank] = (int32_t)r;
+    slot = sm.base[e] + prefix + lane_rank;
+    sorted_ids[slot] = (int32_t)r;
   }
   __syncthreads();
   for (int x = tid; x < E; x += kAlignThreads) {
@@ -61,6 +64,7 @@ __device__ __forceinline__ void scatter_round(int64_t r, int e, int E, AlignSmem
     sm.base[x] += add;
   }
   __syncthreads();
+  return slot;
 }
 
 // Stable scatter of routes [start, end): base[e] holds the next slot of expert e.
@@ -73,9 +77,8 @@ __device__ void stable_scatter(const IT* ids, int64_t start, int64_t end, int E,
   }
 }
 
-// Padded exclusive scan over experts (counts in sm.count) -> sm.off[0..E]; then padding, tail
-// and block -> expert fill.  Called by one CTA.
-__device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
+// Padded exclusive scan over experts (counts in sm.count) -> sm.off[0..E].
+__device__ void padded_scan(const AlignParams& p, AlignSmem& sm) {
   const int tid = threadIdx.x;
   const int E = p.experts;
   const int BM = p.block_size;
@@ -106,16 +109,27 @@ __device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
   if (tid < E) sm.off[tid + 1] = v;
   if (tid == 0) sm.off[0] = 0;
   __syncthreads();
+}
+
+// Padding slots of each expert, the tail past the padded total and the expert of each block,
+// from sm.off and sm.count; the work is split over `parts` CTAs, this one doing part `part`.
+__device__ void fill_padding(const AlignParams& p, const AlignSmem& sm, int part, int parts) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int E = p.experts;
+  const int BM = p.block_size;
   const int total = sm.off[E];
   // padding slots of each expert, one warp per expert
-  for (int e = warp; e < E; e += kAlignWarps) {
+  for (int e = part * kAlignWarps + warp; e < E; e += parts * kAlignWarps) {
     const int q0 = sm.off[e] + sm.count[e], q1 = sm.off[e + 1];
     for (int q = q0 + lane; q < q1; q += 32) p.sorted_ids[q] = (int32_t)p.numel;
   }
-  for (int64_t q = total + tid; q < p.capacity; q += kAlignThreads) p.sorted_ids[q] = (int32_t)p.numel;
+  const int64_t stride = (int64_t)parts * kAlignThreads;
+  const int64_t first = (int64_t)part * kAlignThreads + tid;
+  for (int64_t q = total + first; q < p.capacity; q += stride) p.sorted_ids[q] = (int32_t)p.numel;
   const int64_t nblocks = (p.capacity + BM - 1) / BM;
   const int used = total / BM;
-  for (int64_t b = tid; b < nblocks; b += kAlignThreads) {
+  for (int64_t b = first; b < nblocks; b += stride) {
     int e = -1;
     if (b < used) {
       const int start = (int)b * BM;
@@ -128,7 +142,13 @@ __device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
     }
     p.expert_ids[b] = e;
   }
-  if (tid == 0) *p.num_post_pad = total;
+  if (part == 0 && tid == 0) *p.num_post_pad = total;
+}
+
+// Padded scan and fill by one CTA.
+__device__ void scan_and_fill(const AlignParams& p, AlignSmem& sm) {
+  padded_scan(p, sm);
+  fill_padding(p, sm, 0, 1);
 }
 
 template <typename IT>
@@ -157,6 +177,59 @@ __global__ void __launch_bounds__(kAlignThreads, 1) align_small_kernel(const Ali
 #pragma unroll
   for (int j = 0; j < kPer; ++j)
     if (j < rounds) scatter_round((int64_t)j * kAlignThreads + tid, ex[j], p.experts, sm, p.sorted_ids);
+}
+
+// moe_align fused with the gather of token rows (numel <= kAlignSmall, the expert layer at
+// decode): every CTA counts all routes (they are few; an L2-resident read) and places only its
+// own slice [s0, s0 + slice) of consecutive routes, at the slots the one-CTA kernel gives them
+// (routes of an expert in earlier slices come first, then the slice's own in flat order); then
+// it copies the token row of each route it placed: xs[slot] = x[route / top_k] (16-byte
+// vectors).  Padding, tail and block names are split over the CTAs.  CTA 0 also zeroes
+// zero[0, zero_n) (the expert layer kernel's tile counters).
+template <typename IT>
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_gather_kernel(const AlignParams p, const uint4* __restrict__ x, int top_k, int row_vecs,
+                        uint4* __restrict__ xs, int slice, int32_t* zero, int zero_n) {
+  __shared__ AlignSmem sm;
+  __shared__ int slot_of[kAlignThreads];
+  const IT* ids = static_cast<const IT*>(p.ids);
+  const int tid = threadIdx.x;
+  const int E = p.experts;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (blockIdx.x == 0)
+    for (int i = tid; i < zero_n; i += kAlignThreads) zero[i] = 0;  // the expert layer's counters
+  const int64_t s0 = (int64_t)blockIdx.x * slice;
+  const int64_t s1 = s0 + slice < p.numel ? s0 + slice : p.numel;
+  for (int e = tid; e < E; e += kAlignThreads) {
+    sm.count[e] = 0;
+    sm.base[e] = 0;
+  }
+  __syncthreads();
+  for (int64_t r = tid; r < p.numel; r += kAlignThreads) {
+    const int e = expert_of(ids, r, p.numel, E);
+    if (e >= 0) {
+      atomicAdd(&sm.count[e], 1);
+      if (r < s0) atomicAdd(&sm.base[e], 1);  // routes of e placed by earlier slices
+    }
+  }
+  __syncthreads();
+  padded_scan(p, sm);
+  for (int e = tid; e < E; e += kAlignThreads) sm.base[e] += sm.off[e];
+  __syncthreads();
+  fill_padding(p, sm, blockIdx.x, gridDim.x);
+  for (int64_t r0 = s0; r0 < s1; r0 += kAlignThreads) {
+    slot_of[tid] = scatter_round(r0 + tid, expert_of(ids, r0 + tid, s1, E), E, sm, p.sorted_ids);
+    __syncthreads();
+    const int n = s1 - r0 < kAlignThreads ? (int)(s1 - r0) : kAlignThreads;
+    for (int i = tid; i < n * row_vecs; i += kAlignThreads) {
+      const int k = i / row_vecs;
+      const int c = i - k * row_vecs;
+      const int slot = slot_of[k];
+      if (slot >= 0) xs[(int64_t)slot * row_vecs + c] = x[(r0 + k) / top_k * row_vecs + c];
+    }
+    __syncthreads();  // slot_of is rewritten by the next round
+  }
 }
 
 template <typename IT>
@@ -270,6 +343,31 @@ static cudaError_t launch_align_t(AlignParams p, cudaStream_t s) {
 
 cudaError_t launch_align(int id_dtype, const AlignParams& p, cudaStream_t s) {
   return id_dtype == EXF_I32 ? launch_align_t<int32_t>(p, s) : launch_align_t<int64_t>(p, s);
+}
+
+int64_t align_gather_max_numel() { return kAlignSmall; }
+
+cudaError_t launch_align_gather(const AlignParams& p, const void* x, int top_k, int hidden,
+                                void* xs, int32_t* zero, int zero_n, cudaStream_t s) {
+  if (p.numel < 1 || p.numel > kAlignSmall || hidden % 8 != 0) return cudaErrorInvalidValue;
+  // slices of at least 16 routes, one CTA each, at most one CTA per SM
+  const int sms = sm_count() > 0 ? sm_count() : 1;
+  int64_t slice = (p.numel + sms - 1) / sms;
+  if (slice < 16) slice = 16;
+  const unsigned grid = (unsigned)((p.numel + slice - 1) / slice);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kAlignThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, align_gather_kernel<int32_t>, p, static_cast<const uint4*>(x),
+                         top_k, hidden / 8, static_cast<uint4*>(xs), (int)slice, zero, zero_n);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace exf

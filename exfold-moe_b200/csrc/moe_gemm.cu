@@ -18,8 +18,9 @@
 // the epilogue.  Two TMEM accumulators (all 512 columns) let the epilogue of one tile overlap
 // the mainloop of the next.  The N tiles of one M block run side by side on neighbouring CTAs,
 // so A tiles and the expert's weight tiles are reused from L2.
-// Decode (expert_gemm_t_kernel, experts holding 64 routes or fewer on average): weight rows on
-// the M side, blocks of 64 routes on the N side (see the comment above that kernel).
+// Decode (expert_layer_t_kernel, experts holding 64 routes or fewer on average): both GEMMs in
+// one persistent launch, weight rows on the M side, blocks of 64 routes on the N side (see the
+// comment above that kernel).
 // Every mbarrier wait is bounded: on time-out the CTA records an error in *status, skips the
 // rest of its work, still frees its TMEM and returns.
 #include <cuda.h>
@@ -260,56 +261,118 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0 && sm.failed && p.status) atomicExch(p.status, 1);
 }
 
-// ---- decode: routes on the N side -------------------------------------------------------------
+// ---- decode: one persistent kernel for the whole expert layer, routes on the N side ------------
 // At decode an expert holds a few routes, so a 128-row block of routes is mostly padding, and the
-// MMA work of that padding, not the weight stream, bounds the layer (with the weight loads taken
-// out, the Qwen3 decode layer took 169 us instead of 160).  Here a tile is 128 weight rows of one
-// expert (the M side, all real) times a block of BT = 64 of its routes (the N side; the moe_align
-// block size of this path), so the MMA work follows the real routes and 80 % of each GEMM-1
-// pipeline stage is weights.
-//   GEMM-1: Dg[f][r] = W1[e][f] . xs[r] and Du[f][r] = W3[e][f] . xs[r] in two accumulators; the
-//           epilogue writes act[r][f] = silu(Dg) * Du for the block's real routes;
-//   GEMM-2: D[h][r] = W2[e][h] . act[r]; the epilogue writes out[route][h] = w_route * D.
-// Tiles t = block * feature_tiles + feature_tile: the CTAs running at one time stream neighbouring
-// row slabs of a few experts' weights (block-major measured 4-12 % faster than feature-tile-major,
-// which spreads them over as many experts as CTAs).  Roles, pipeline, TMEM double buffering and
-// bounded waits as in expert_gemm_kernel.
-template <int KIND, int BT>
-struct TCfg {
+// MMA work of that padding, not the weight stream, bounds the layer.  Here a tile is 256 weight
+// rows of one expert (two 128-row MMA tiles on the M side, all real) times a block of BT = 64 of
+// its routes (the N side; the moe_align block size of this path):
+//   GEMM-1 tile (block, f): gate rows [128 f, +128) and up rows [I + 128 f, +128) of W13[e]
+//     against the block's gathered token rows xs, K = H; the epilogue writes
+//     act[r][128 f + i] = silu(gate) * up for the block's real routes;
+//   GEMM-2 tile (block, f): rows [256 f, +256) of W2[e] against act, K = I; the epilogue writes
+//     out[route][256 f + i] = w_route * D.
+// Every pipeline stage holds two 16 KB weight tiles and one 8 KB route tile (80 % weights), in
+// both GEMMs.  One launch runs both GEMMs so that no SM idles at the end of GEMM-1 (its 1 MB
+// tiles come in few rounds per SM): warp 0 takes tiles from a counter shared by all CTAs, all
+// GEMM-1 tiles first, block by block, then the GEMM-2 tiles; before loading act for a GEMM-2
+// tile it waits until every epilogue warp that wrote the block's act rows has counted itself off
+// (release / acquire on sync[1 + block], with proxy fences: act is written by plain stores and
+// read by TMA).  A GEMM-1 tile never waits for anything but earlier tiles of its own CTA, so the
+// GEMM-1 tiles a GEMM-2 tile needs always finish: each was handed out earlier to a running CTA
+// whose producer had issued all of its loads before taking another tile.  Warp 0 passes tile
+// numbers to the MMA warp and the epilogue warps through a ring in shared memory.  Roles, the
+// stage ring, TMEM double buffering and bounded waits otherwise as in expert_gemm_kernel; a
+// time-out anywhere marks the CTA failed, and the rest of the CTA drains and returns.
+struct ExpertLayerParams {
+  const int32_t* num_post_pad;
+  const int32_t* expert_ids;   // [m_blocks]
+  const int32_t* sorted_ids;   // [m_blocks * BT]
+  int experts;
+  int numel;
+  int hidden;
+  int inter;
+  int m_blocks;
+  int* status;
+  __nv_bfloat16* act;          // [m_blocks * BT][inter]
+  const float* route_w;        // [numel]
+  __nv_bfloat16* out;          // [numel][hidden]
+  int32_t* sync;               // [0] next tile; [1 + b] GEMM-1 epilogue warps done with block b
+};
+
+template <int BT>
+struct LCfg {
   static constexpr int kWTile = 128 * kBK * 2;   // 16 KB: 128 weight rows x 64 K
   static constexpr int kTTile = BT * kBK * 2;    // BT route rows x 64 K
-  static constexpr int kWTiles = KIND == kGemmSwiGLU ? 2 : 1;   // gate and up, or W2
-  static constexpr int kStageBytes = kWTiles * kWTile + kTTile;
+  static constexpr int kStageBytes = 2 * kWTile + kTTile;
   static constexpr int kStages = (200 * 1024) / kStageBytes;
-  static constexpr int kAccCols = kWTiles * BT;  // TMEM columns of one tile's accumulators
-  static constexpr int kTmemCols = 2 * kAccCols; // two tiles in flight: 64 .. 256, a power of 2
+  static constexpr int kAccCols = 2 * BT;        // two M tiles of BT columns
+  static constexpr int kTmemCols = 2 * kAccCols; // two tiles in flight
+  static constexpr int kRing = 8;                // tile numbers handed to the MMA and epilogue
   static constexpr uint32_t kIdesc = idesc_f16(128, BT, true);  // bf16, M = 128, N = BT
 };
 
-template <int KIND, int BT>
-struct TSmem {
-  alignas(1024) uint8_t tiles[TCfg<KIND, BT>::kStages][TCfg<KIND, BT>::kStageBytes];
-  alignas(8) uint64_t full[TCfg<KIND, BT>::kStages];
-  alignas(8) uint64_t empty[TCfg<KIND, BT>::kStages];
+template <int BT>
+struct LSmem {
+  alignas(1024) uint8_t tiles[LCfg<BT>::kStages][LCfg<BT>::kStageBytes];
+  alignas(8) uint64_t full[LCfg<BT>::kStages];
+  alignas(8) uint64_t empty[LCfg<BT>::kStages];
   alignas(8) uint64_t acc_full[2];
   alignas(8) uint64_t acc_empty[2];
+  alignas(8) uint64_t ring_full[LCfg<BT>::kRing];
+  alignas(8) uint64_t ring_empty[LCfg<BT>::kRing];
   alignas(8) uint64_t drain;
+  int ring[LCfg<BT>::kRing];
   uint32_t tmem_base;
   int failed;
 };
-template <int KIND, int BT>
-constexpr size_t tgemm_smem_bytes() { return sizeof(TSmem<KIND, BT>) + 1024; }
-static_assert(tgemm_smem_bytes<kGemmSwiGLU, 64>() <= 232448, "decode GEMM shared memory");
-static_assert(tgemm_smem_bytes<kGemmDown, 64>() <= 232448, "decode GEMM shared memory");
+template <int BT>
+constexpr size_t layer_smem_bytes() { return sizeof(LSmem<BT>) + 1024; }
+static_assert(layer_smem_bytes<64>() <= 232448, "decode expert layer shared memory");
 
-template <int KIND, int BT>
+// Tile t of the layer over `blocks` route blocks: GEMM-1 tiles [0, blocks * n1) block-major,
+// then GEMM-2 tiles block-major.
+struct LayerTile {
+  int kind;   // kGemmSwiGLU or kGemmDown
+  int blk;
+  int ft;
+};
+__device__ __forceinline__ LayerTile layer_tile(int t, int blocks, int n1, int n2) {
+  LayerTile r;
+  const int s_tiles = blocks * n1;
+  if (t < s_tiles) {
+    r.kind = kGemmSwiGLU;
+    r.blk = t / n1;
+    r.ft = t - r.blk * n1;
+  } else {
+    t -= s_tiles;
+    r.kind = kGemmDown;
+    r.blk = t / n2;
+    r.ft = t - r.blk * n2;
+  }
+  return r;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int32_t* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int BT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    expert_gemm_t_kernel(const __grid_constant__ CUtensorMap map_w,
-                         const __grid_constant__ CUtensorMap map_t, const ExpertGemmParams p) {
-  using C = TCfg<KIND, BT>;
+    expert_layer_t_kernel(const __grid_constant__ CUtensorMap map_w13,
+                          const __grid_constant__ CUtensorMap map_xs,
+                          const __grid_constant__ CUtensorMap map_w2,
+                          const __grid_constant__ CUtensorMap map_act,
+                          const ExpertLayerParams p) {
+  using C = LCfg<BT>;
   constexpr int kStages = C::kStages;
+  constexpr int kRing = C::kRing;
   extern __shared__ uint8_t smem_raw[];
-  TSmem<KIND, BT>& sm = *reinterpret_cast<TSmem<KIND, BT>*>(
+  LSmem<BT>& sm = *reinterpret_cast<LSmem<BT>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -323,6 +386,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
     }
+    for (int j = 0; j < kRing; ++j) {
+      mbar_init(&sm.ring_full[j], 1);
+      mbar_init(&sm.ring_empty[j], 5);  // the MMA thread and the four epilogue warps
+    }
     mbar_init(&sm.drain, 1);
     sm.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -335,44 +402,71 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int post = *p.num_post_pad;
-  const int m_used = (post + BT - 1) / BT < p.m_blocks ? (post + BT - 1) / BT : p.m_blocks;
-  const int ntiles = m_used * p.n_tiles;
-  auto tile_expert = [&](int t, int& blk, int& ft) {
-    blk = t / p.n_tiles;
-    ft = t - blk * p.n_tiles;
-    const int e = p.expert_ids[blk];
-    return (e >= 0 && e < p.experts) ? e : -1;
-  };
+  const int blocks = (post + BT - 1) / BT < p.m_blocks ? (post + BT - 1) / BT : p.m_blocks;
+  const int n1 = p.inter / 128;  // GEMM-1 tiles per block
+  const int n2 = p.hidden / 256; // GEMM-2 tiles per block
+  const int total = blocks * (n1 + n2);
   const uint32_t tmem = sm.tmem_base;
   volatile int* failed = &sm.failed;
-  const int kblocks = p.k / kBK;
+  auto expert_of = [&](const LayerTile& lt) {
+    const int e = p.expert_ids[lt.blk];
+    return (e >= 0 && e < p.experts) ? e : -1;
+  };
 
   if (warp == 0) {
-    // ---- TMA producer
+    // ---- scheduler + TMA producer (one thread)
     if (lane == 0) {
-      uint32_t g = 0;
+      uint32_t g = 0;  // stages issued
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        int blk, ft;
-        const int expert = tile_expert(t, blk, ft);
+      int t = atomicAdd(p.sync, 1);
+      for (int j = 0; ok; ++j) {
+        const int tile = t < total ? t : -1;
+        const int slot = j % kRing;
+        ok = mbar_wait(&sm.ring_empty[slot], ((j / kRing) & 1) ^ 1, failed);
+        if (!ok) break;
+        sm.ring[slot] = tile;
+        mbar_arrive(&sm.ring_full[slot]);
+        if (tile < 0) break;
+        t = atomicAdd(p.sync, 1);  // the next tile: its latency overlaps this tile's loads
+        const LayerTile lt = layer_tile(tile, blocks, n1, n2);
+        const int expert = expert_of(lt);
         if (expert < 0) continue;
+        const bool down = lt.kind == kGemmDown;
+        if (down) {
+          // act rows of the block: every epilogue warp of its n1 GEMM-1 tiles has counted itself
+          // off (bounded wait; the GEMM-1 tiles were handed out earlier to running CTAs)
+          const int32_t* flag = p.sync + 1 + lt.blk;
+          const int want = 4 * n1;
+          uint32_t it = 0;
+          while (ld_acquire_gpu(flag) < want) {
+            if (*failed || ++it >= kWaitLimit) {
+              *failed = 1;
+              ok = false;
+              break;
+            }
+            __nanosleep(128);
+          }
+          if (!ok) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        const int kblocks = (down ? p.inter : p.hidden) / kBK;
+        const CUtensorMap* mw = down ? &map_w2 : &map_w13;
+        const CUtensorMap* mt = down ? &map_act : &map_xs;
+        // the two 128-row weight tiles: gate and up rows of W13[e], or 256 rows of W2[e]
+        const int row0 = down ? expert * p.hidden + lt.ft * 256 : expert * 2 * p.inter + lt.ft * 128;
+        const int row1 = down ? row0 + 128 : row0 + p.inter;
         for (int kb = 0; kb < kblocks; ++kb, ++g) {
           const int s = g % kStages;
           ok = mbar_wait(&sm.empty[s], ((g / kStages) & 1) ^ 1, failed);
           if (!ok) break;
           uint8_t* st = sm.tiles[s];
           mbar_expect_tx(&sm.full[s], C::kStageBytes);
-          if (KIND == kGemmSwiGLU) {
-            // gate rows [f0, f0 + 128) and up rows [I + f0, I + f0 + 128) of W13[expert]
-            const int row0 = expert * 2 * p.n_total + ft * 128;
-            tma_load_2d(st, &map_w, &sm.full[s], kb * kBK, row0);
-            tma_load_2d(st + C::kWTile, &map_w, &sm.full[s], kb * kBK, row0 + p.n_total);
-          } else {
-            tma_load_2d(st, &map_w, &sm.full[s], kb * kBK, expert * p.n_total + ft * 128);
-          }
-          tma_load_2d(st + C::kWTiles * C::kWTile, &map_t, &sm.full[s], kb * kBK, blk * BT);
+          tma_load_2d(st, mw, &sm.full[s], kb * kBK, row0);
+          tma_load_2d(st + C::kWTile, mw, &sm.full[s], kb * kBK, row1);
+          tma_load_2d(st + 2 * C::kWTile, mt, &sm.full[s], kb * kBK, lt.blk * BT);
         }
       }
+      // (after a failure the consumers leave their waits on the failed flag)
       for (uint32_t j = g > kStages ? g - kStages : 0; j < g; ++j)
         mbar_wait_drain(&sm.full[j % kStages], (j / kStages) & 1);
     }
@@ -382,9 +476,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t g = 0;
       int i = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        int blk, ft;
-        if (tile_expert(t, blk, ft) < 0) continue;
+      for (int j = 0; ok; ++j) {
+        const int slot = j % kRing;
+        ok = mbar_wait(&sm.ring_full[slot], (j / kRing) & 1, failed);
+        if (!ok) break;
+        const int tile = sm.ring[slot];
+        mbar_arrive(&sm.ring_empty[slot]);
+        if (tile < 0) break;
+        const LayerTile lt = layer_tile(tile, blocks, n1, n2);
+        if (expert_of(lt) < 0) continue;
+        const int kblocks = (lt.kind == kGemmDown ? p.inter : p.hidden) / kBK;
         const int b = i & 1;
         ok = mbar_wait(&sm.acc_empty[b], ((i >> 1) & 1) ^ 1, failed);
         if (!ok) break;
@@ -396,15 +497,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!ok) break;
           fence_after_sync();
           const uint32_t w_base = smem_addr(sm.tiles[s]);
-          const uint32_t t_base = w_base + C::kWTiles * C::kWTile;
+          const uint32_t t_base = w_base + 2 * C::kWTile;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint32_t on = (kb > 0 || k > 0) ? 1u : 0u;
             mma_kind_f16(acc, smem_desc(w_base + k * 32), smem_desc(t_base + k * 32), C::kIdesc,
                          on);
-            if (KIND == kGemmSwiGLU)
-              mma_kind_f16(acc + BT, smem_desc(w_base + C::kWTile + k * 32),
-                           smem_desc(t_base + k * 32), C::kIdesc, on);
+            mma_kind_f16(acc + BT, smem_desc(w_base + C::kWTile + k * 32),
+                         smem_desc(t_base + k * 32), C::kIdesc, on);
           }
           mma_commit(&sm.empty[s]);
         }
@@ -416,47 +516,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait_drain(&sm.drain, 0);
     }
   } else {
-    // ---- epilogue: warps 2-5 own TMEM lanes 32 (warp % 4) .. +31 = 32 weight rows (features);
-    // columns are the block's routes.  Lane j fetches route j of each 32-route chunk and shares it.
+    // ---- epilogue: warps 2-5 own TMEM lanes 32 (warp % 4) .. +31, i.e. 32 weight rows of each
+    // M tile; columns are the block's routes.  Lane j fetches route j of each 32-route chunk and
+    // shares it.
     const int q = warp & 3;
     int i = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      int blk, ft;
-      if (tile_expert(t, blk, ft) < 0) continue;
+    for (int j = 0;; ++j) {
+      const int slot = j % kRing;
+      int tile = -2;  // -2: the wait failed
+      if (lane == 0 && mbar_wait(&sm.ring_full[slot], (j / kRing) & 1, failed)) {
+        tile = sm.ring[slot];
+        mbar_arrive(&sm.ring_empty[slot]);
+      }
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      if (tile < 0) break;
+      const LayerTile lt = layer_tile(tile, blocks, n1, n2);
+      if (expert_of(lt) < 0) continue;
       const int b = i & 1;
       const bool ok = mbar_wait(&sm.acc_full[b], (i >> 1) & 1, failed);
       fence_after_sync();
       if (!ok || *failed) break;
-      const int feat = ft * 128 + q * 32 + lane;
       const uint32_t taddr =
           tmem + static_cast<uint32_t>(b * C::kAccCols) + ((uint32_t)(q * 32) << 16);
+      if (lt.kind == kGemmSwiGLU) {
+        const int feat = lt.ft * 128 + q * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < BT; c += 32) {
-        const int row_l = blk * BT + c + lane;  // this lane's route row of the chunk
-        const int route_l = p.sorted_ids[row_l];
-        const bool real_l = route_l < p.numel;
-        if (KIND == kGemmSwiGLU) {
+        for (int c = 0; c < BT; c += 32) {
+          const bool real_l = p.sorted_ids[lt.blk * BT + c + lane] < p.numel;
           float gt[32], up[32];
           tmem_load32(taddr + c, gt);
           tmem_load32(taddr + BT + c, up);
-          __nv_bfloat16* dst = p.act + (int64_t)(blk * BT + c) * p.n_total + feat;
+          __nv_bfloat16* dst = p.act + (int64_t)(lt.blk * BT + c) * p.inter + feat;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const bool real = __shfl_sync(0xffffffffu, real_l, j);
+          for (int r = 0; r < 32; ++r) {
+            const bool real = __shfl_sync(0xffffffffu, real_l, r);
             if (real)
-              dst[(int64_t)j * p.n_total] =
-                  __float2bfloat16_rn(gt[j] / (1.0f + __expf(-gt[j])) * up[j]);
+              dst[(int64_t)r * p.inter] =
+                  __float2bfloat16_rn(gt[r] / (1.0f + __expf(-gt[r])) * up[r]);
           }
-        } else {
-          const float w_l = real_l ? p.route_w[route_l] : 0.0f;
-          float v[32];
-          tmem_load32(taddr + c, v);
+        }
+      } else {
+        const int feat = lt.ft * 256 + q * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BT; c += 32) {
+          const int route_l = p.sorted_ids[lt.blk * BT + c + lane];
+          const float w_l = route_l < p.numel ? p.route_w[route_l] : 0.0f;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {  // the two M tiles: features feat and feat + 128
+            float v[32];
+            tmem_load32(taddr + h * BT + c, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int route = __shfl_sync(0xffffffffu, route_l, j);
-            const float wr = __shfl_sync(0xffffffffu, w_l, j);
-            if (route < p.numel)
-              p.out[(int64_t)route * p.hidden + feat] = __float2bfloat16_rn(v[j] * wr);
+            for (int r = 0; r < 32; ++r) {
+              const int route = __shfl_sync(0xffffffffu, route_l, r);
+              const float wr = __shfl_sync(0xffffffffu, w_l, r);
+              if (route < p.numel)
+                p.out[(int64_t)route * p.hidden + feat + h * 128] = __float2bfloat16_rn(v[r] * wr);
+            }
           }
         }
       }
@@ -464,6 +579,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
       ++i;
+      if (lt.kind == kGemmSwiGLU) {
+        // this warp's act rows of the tile are written: make them visible to the TMA loads of
+        // the block's GEMM-2 tiles (any CTA), then count the warp off
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_gpu_add(p.sync + 1 + lt.blk, 1);
+      }
     }
   }
   fence_before_sync();
@@ -477,16 +600,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---- gather and combine ---------------------------------------------------------------------
-// xs[m] = x[sorted_ids[m] / top_k] for the real routes of the used rows (16-byte vectors).
+// xs[m] = x[sorted_ids[m] / top_k] for the real routes of the used rows (16-byte vectors); also
+// zeroes zero[0, zero_n).
 // Padding rows keep whatever the workspace holds: the GEMM rows are independent, GEMM-1's
 // padding rows only feed GEMM-2's padding rows, and those are never stored.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* x,
                                                           const int32_t* sorted_ids,
                                                           const int32_t* num_post_pad,
                                                           int64_t rows, int numel, int top_k,
-                                                          int hidden, __nv_bfloat16* xs) {
+                                                          int hidden, __nv_bfloat16* xs,
+                                                          int32_t* zero, int zero_n) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < zero_n; i += gridDim.x * blockDim.x)
+    zero[i] = 0;  // the decode expert layer kernel's counters
   const int vec = hidden / 8;
   const int64_t used = *num_post_pad < rows ? *num_post_pad : rows;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < used * vec;
@@ -547,12 +674,9 @@ static cudaError_t allow_gemm_smem() {
   std::lock_guard<std::mutex> lock(mu);
   if (done[dev]) return cudaSuccess;
   const int s256 = (int)gemm_smem_bytes<256>();
-  if ((e = cudaFuncSetAttribute(expert_gemm_t_kernel<kGemmSwiGLU, 64>,
+  if ((e = cudaFuncSetAttribute(expert_layer_t_kernel<64>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)tgemm_smem_bytes<kGemmSwiGLU, 64>())) != cudaSuccess ||
-      (e = cudaFuncSetAttribute(expert_gemm_t_kernel<kGemmDown, 64>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)tgemm_smem_bytes<kGemmDown, 64>())) != cudaSuccess ||
+                                (int)layer_smem_bytes<64>())) != cudaSuccess ||
       (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmSwiGLU, 256>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, s256)) != cudaSuccess ||
       (e = cudaFuncSetAttribute(expert_gemm_kernel<kGemmDown, 256>,
@@ -618,6 +742,8 @@ MoeWorkspace moe_workspace(int64_t tokens, int top_k, int experts, int hidden, i
   w.xs = reinterpret_cast<__nv_bfloat16*>(take(cap * hidden * 2));
   w.act = reinterpret_cast<__nv_bfloat16*>(take(cap * inter * 2));
   w.out = reinterpret_cast<__nv_bfloat16*>(take(numel * hidden * 2));
+  w.layer_sync_ints = (int)(1 + cap / 64);
+  w.layer_sync = reinterpret_cast<int32_t*>(take(w.layer_sync_ints * 4));
   w.bytes = off;
   return w;
 }
@@ -660,43 +786,34 @@ static cudaError_t launch_gemms(const MoeArgs& a, const MoeWorkspace& w, cudaStr
                     s, ma, mb, p);
 }
 
-// GEMM-1 and GEMM-2 with the routes on the N side (decode; see expert_gemm_t_kernel), over routes
-// aligned into blocks of BT.
+// The decode expert layer (both GEMMs, routes on the N side; see expert_layer_t_kernel) over
+// routes aligned into blocks of BT.
 template <int BT>
-static cudaError_t launch_gemms_t(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+static cudaError_t launch_layer_t(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
   const int64_t cap = w.capacity;
-  CUtensorMap mw, mt;
-  if (!make_map(&mw, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, 128) ||
-      !make_map(&mt, w.xs, cap, a.hidden, BT))
+  CUtensorMap m13, mxs, m2, mact;
+  if (!make_map(&m13, a.w13, (uint64_t)a.experts * 2 * a.inter, a.hidden, 128) ||
+      !make_map(&mxs, w.xs, cap, a.hidden, BT) ||
+      !make_map(&m2, a.w2, (uint64_t)a.experts * a.hidden, a.inter, 128) ||
+      !make_map(&mact, w.act, cap, a.inter, BT))
     return cudaErrorInvalidValue;
-  ExpertGemmParams p{};
+  ExpertLayerParams p{};
   p.num_post_pad = w.num_post_pad;
   p.expert_ids = w.expert_ids;
   p.sorted_ids = w.sorted_ids;
   p.experts = a.experts;
   p.numel = (int)(a.tokens * a.top_k);
   p.hidden = a.hidden;
-  p.status = a.status;
-  p.k = a.hidden;
-  p.n_total = a.inter;
-  p.act = w.act;
+  p.inter = a.inter;
   p.m_blocks = (int)(cap / BT);
-  p.n_tiles = a.inter / 128;
-  const int sms = sm_count();
-  const unsigned grid = sms > 0 ? (unsigned)sms : 1u;
-  cudaError_t e = launch_pdl(expert_gemm_t_kernel<kGemmSwiGLU, BT>, grid, kGemmThreads,
-                             tgemm_smem_bytes<kGemmSwiGLU, BT>(), s, mw, mt, p);
-  if (e != cudaSuccess) return e;
-  if (!make_map(&mw, a.w2, (uint64_t)a.experts * a.hidden, a.inter, 128) ||
-      !make_map(&mt, w.act, cap, a.inter, BT))
-    return cudaErrorInvalidValue;
-  p.k = a.inter;
-  p.n_total = a.hidden;
+  p.status = a.status;
+  p.act = w.act;
   p.route_w = a.topk_w;
   p.out = w.out;
-  p.n_tiles = a.hidden / 128;
-  return launch_pdl(expert_gemm_t_kernel<kGemmDown, BT>, grid, kGemmThreads,
-                    tgemm_smem_bytes<kGemmDown, BT>(), s, mw, mt, p);
+  p.sync = w.layer_sync;
+  const int sms = sm_count();
+  return launch_pdl(expert_layer_t_kernel<BT>, sms > 0 ? (unsigned)sms : 1u, kGemmThreads,
+                    layer_smem_bytes<BT>(), s, m13, mxs, m2, mact, p);
 }
 
 // The moe_align block size, which also picks the GEMM kernels: 128-row blocks of routes on the M
@@ -709,45 +826,54 @@ static int gemm_block(int64_t numel, int experts) {
   return numel > (int64_t)experts * 64 ? kBM : kDecodeBlock;
 }
 
+// Steps 3-5 of launch_moe_experts: GEMM-1 + SwiGLU, GEMM-2, combine, from token rows already
+// gathered into w.xs in the order of routes aligned into blocks of gemm_block.
+static cudaError_t launch_moe_gemms(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
+  cudaError_t e = allow_gemm_smem();
+  if (e != cudaSuccess) return e;
+  // 3-4. GEMM-1 + SwiGLU, GEMM-2
+  e = gemm_block(a.tokens * a.top_k, a.experts) == kDecodeBlock
+          ? launch_layer_t<kDecodeBlock>(a, w, s)
+          : launch_gemms<256>(a, w, s);
+  if (e != cudaSuccess) return e;
+  // 5. combine the routes of each token
+  const int64_t work = a.tokens * (a.hidden / 8);
+  int64_t blocks = (work + 255) / 256;
+  const int lim = 8 * sm_count();
+  if (lim > 0 && blocks > lim) blocks = lim;
+  return launch_pdl(combine_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
+                    static_cast<const __nv_bfloat16*>(w.out), a.topk_ids, a.experts, a.tokens,
+                    a.top_k, a.hidden, static_cast<__nv_bfloat16*>(a.y));
+}
+
 // Steps 2-5 of launch_moe_experts, from routes already aligned into w (blocks of gemm_block).
 static cudaError_t launch_moe_compute(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
   const int64_t numel = a.tokens * a.top_k;
   const int64_t cap = w.capacity;
-  cudaError_t e = allow_gemm_smem();
-  if (e != cudaSuccess) return e;
   // 2. gather token rows into route order
-  {
-    const int64_t work = cap * (a.hidden / 8);
-    int64_t blocks = (work + 255) / 256;
-    const int lim = 8 * sm_count();
-    if (lim > 0 && blocks > lim) blocks = lim;
-    e = launch_pdl(gather_rows_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
-                   static_cast<const __nv_bfloat16*>(a.x), static_cast<const int32_t*>(w.sorted_ids),
-                   static_cast<const int32_t*>(w.num_post_pad), cap, (int)numel, a.top_k, a.hidden,
-                   w.xs);
-    if (e != cudaSuccess) return e;
-  }
-  // 3-4. GEMM-1 + SwiGLU, GEMM-2
-  e = gemm_block(numel, a.experts) == kDecodeBlock ? launch_gemms_t<kDecodeBlock>(a, w, s)
-                                                   : launch_gemms<256>(a, w, s);
-  if (e != cudaSuccess) return e;
-  // 5. combine the routes of each token
-  {
-    const int64_t work = a.tokens * (a.hidden / 8);
-    int64_t blocks = (work + 255) / 256;
-    const int lim = 8 * sm_count();
-    if (lim > 0 && blocks > lim) blocks = lim;
-    return launch_pdl(combine_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
-                      static_cast<const __nv_bfloat16*>(w.out), a.topk_ids, a.experts, a.tokens,
-                      a.top_k, a.hidden, static_cast<__nv_bfloat16*>(a.y));
-  }
+  const int64_t work = cap * (a.hidden / 8);
+  int64_t blocks = (work + 255) / 256;
+  const int lim = 8 * sm_count();
+  if (lim > 0 && blocks > lim) blocks = lim;
+  const cudaError_t e =
+      launch_pdl(gather_rows_kernel, (unsigned)(blocks > 0 ? blocks : 1), 256, 0, s,
+                 static_cast<const __nv_bfloat16*>(a.x), static_cast<const int32_t*>(w.sorted_ids),
+                 static_cast<const int32_t*>(w.num_post_pad), cap, (int)numel, a.top_k, a.hidden,
+                 w.xs, w.layer_sync, w.layer_sync_ints);
+  return e != cudaSuccess ? e : launch_moe_gemms(a, w, s);
 }
 
 cudaError_t launch_moe_experts(const MoeArgs& a, const MoeWorkspace& w, cudaStream_t s) {
-  // 1. moe_align with the GEMM's blocks
-  AlignParams ap{a.topk_ids, a.tokens * a.top_k, a.experts,
-                 gemm_block(a.tokens * a.top_k, a.experts), w.capacity, w.sorted_ids,
-                 w.expert_ids, w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
+  // 1-2. moe_align with the GEMM's blocks, then the gather of token rows; at decode sizes both
+  // in one launch of one CTA per SM
+  const int64_t numel = a.tokens * a.top_k;
+  AlignParams ap{a.topk_ids, numel, a.experts, gemm_block(numel, a.experts), w.capacity,
+                 w.sorted_ids, w.expert_ids, w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
+  if (numel <= align_gather_max_numel()) {
+    const cudaError_t e = launch_align_gather(ap, a.x, a.top_k, a.hidden, w.xs, w.layer_sync,
+                                              w.layer_sync_ints, s);
+    return e != cudaSuccess ? e : launch_moe_gemms(a, w, s);
+  }
   const cudaError_t e = launch_align(0 /*int32*/, ap, s);
   return e != cudaSuccess ? e : launch_moe_compute(a, w, s);
 }

@@ -2,7 +2,10 @@
 
 The reference computes every route in fp32 from the same bf16 inputs, rounds the SwiGLU
 activation to bf16 as the kernel (and vLLM's intermediate cache) does, and sums the weighted
-routes.  Tolerance: bf16, 2e-2 relative to the output scale.
+routes; routes whose expert id is out of range contribute nothing.  Tolerance: bf16, 2e-2
+relative to the output scale.  Both kernel paths are covered: blocks of 128 routes on the M side
+(many routes per expert) and blocks of 64 routes on the N side with the combine inside GEMM-2
+(64 routes per expert or fewer on average).
 """
 
 from __future__ import annotations
@@ -22,6 +25,8 @@ def reference(x, topk_w, topk_ids, w13, w2):
     y = torch.zeros(tokens, hidden, dtype=torch.float32, device=x.device)
     xf = x.float()
     for e in torch.unique(topk_ids).tolist():
+        if e < 0 or e >= w13.shape[0]:
+            continue  # routes of an expert id out of range are dropped
         rows, slots = torch.nonzero(topk_ids == e, as_tuple=True)
         h = xf[rows]
         w = w13[e].float()
@@ -94,4 +99,28 @@ def test_prefill_many_rows_per_expert():
 def test_deterministic():
     a, _ = run_case(tokens=200, experts=16, top_k=4, hidden=512, inter=256, seed=6)
     b, _ = run_case(tokens=200, experts=16, top_k=4, hidden=512, inter=256, seed=6)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("tokens,experts,top_k", [(300, 32, 4), (3000, 8, 4)])
+def test_invalid_and_duplicate_expert_ids(tokens, experts, top_k):
+    """Ids of -1 and >= experts are skipped; a token with no valid id gets y = 0; an expert named
+    twice by one token counts twice.  (300, 32, 4) takes the decode kernels, (3000, 8, 4) the
+    prefill ones."""
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(77)
+    logits = torch.randn(tokens, experts, generator=gen, device=DEV)
+    ids = logits.topk(top_k, dim=-1).indices.to(torch.int32)
+    ids[0, :] = -1
+    ids[1, 1] = experts
+    ids[2, 1] = ids[2, 0]
+    ids[3, :] = 5
+    ids[4, :] = torch.tensor([-1, experts + 7, 3, -1], dtype=torch.int32)
+    y, _ = run_case(tokens, experts, top_k, hidden=512, inter=256, seed=78, ids=ids)
+    assert torch.count_nonzero(y[0]).item() == 0
+
+
+def test_deterministic_prefill_path():
+    a, _ = run_case(tokens=2000, experts=8, top_k=4, hidden=512, inter=256, seed=9)
+    b, _ = run_case(tokens=2000, experts=8, top_k=4, hidden=512, inter=256, seed=9)
     assert torch.equal(a, b)
