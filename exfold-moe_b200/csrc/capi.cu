@@ -441,6 +441,7 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
   EXF_REQUIRE(tokens >= 0 && top_k >= 1 &&
                   tokens * top_k + (int64_t)experts * 127 < ((int64_t)1 << 31),
               "%s: bad routing shape (routes plus block padding must stay below 2^31)", name);
+  if (top_k > 8) return fail(EXF_ERR_UNSUPPORTED, "%s: top_k must be at most 8, got %d", name, top_k);
   if (experts < 1 || experts > align_max_experts())
     return fail(EXF_ERR_UNSUPPORTED, "%s: experts must be in [1, %d]", name, align_max_experts());
   if (hidden % 256 != 0 || inter % 128 != 0)

@@ -214,7 +214,8 @@ EXF_API int exf_moe_align(const void* ids, int id_dtype, int64_t numel, int expe
  * [experts][hidden][inter]; y bf16 [tokens][hidden].  The intermediate activation is rounded to
  * bf16 (as vLLM's intermediate cache).  workspace: exf_fused_experts_workspace_bytes(), 16-byte
  * aligned.  status: optional device int32, set to 1 if a pipeline wait timed out.
- * hidden % 256 == 0, inter % 128 == 0, experts <= 512. */
+ * hidden % 256 == 0, inter % 128 == 0, experts <= 512, 1 <= top_k <= 8; routes whose id is
+ * outside [0, experts) contribute nothing. */
 EXF_API int64_t exf_fused_experts_workspace_bytes(int64_t tokens, int top_k, int experts,
                                                   int hidden, int inter);
 EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t* topk_ids,

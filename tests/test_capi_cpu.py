@@ -106,6 +106,10 @@ def test_argument_validation_without_gpu():
     assert dfe(2048, 8, 128, 1 << 30) == L.EXF_ERR_UNSUPPORTED and "8192" in last_error()
     assert dfe(4, 8, 128, 16) == L.EXF_ERR_INVALID and "workspace" in last_error()
     assert dfe(0, 8, 128, 0) == 0
+    # the expert layer sums at most 8 routes per token
+    rc = call("exf_fused_experts", fake, fake, fake, 4, 9, fake, fake, 16, 256, 128, fake, fake,
+              1 << 30, None, None)
+    assert rc == L.EXF_ERR_UNSUPPORTED and "top_k" in last_error()
 
 
 def test_empty_inputs_are_no_ops_without_gpu():
