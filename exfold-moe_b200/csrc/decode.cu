@@ -111,31 +111,32 @@ __device__ void exchange_importance(const DecodeParams& p, DecodeSmem& sm) {
                        ((par * R + me) * E) * 2 + k,
                    tag | half);
   }
+  // the sum is staged in hist (free between phases 1 and 2) so that sm.imp changes only if every
+  // rank's vector arrived
+  for (int e = tid; e < E; e += kDecodeThreads) sm.hist[e] = 0;
   __syncthreads();  // every local read of sm.imp is done before it is overwritten below
-  // poll this rank's slots of parity par; each thread owns whole experts (both halves, all r)
+  // poll this rank's slots of parity par: one (rank, expert) word pair per thread, so that the
+  // first load of every pair is in flight at once; the ranks' values are added into hist[e] with
+  // 64-bit shared atomics (modulo 2^64, as the single-GPU sums: any order gives the same sum)
   const unsigned long long limit = p.wait_ns ? p.wait_ns : kDefaultWaitNs;
   const unsigned long long t0 = global_ns();
   bool late = false;
-  for (int e = tid; e < E; e += kDecodeThreads) {
-    unsigned long long acc = 0;  // modulo 2^64, as the single-GPU sums
-    for (int r = 0; r < R; ++r) {
-      const unsigned long long* wp = own + kXchSlots + ((par * R + r) * E + e) * 2;
-      unsigned long long lo = ld_relaxed_sys(wp), hi = ld_relaxed_sys(wp + 1);
-      // time-bounded, and iteration-bounded too (at least ~4 s of 64 ns sleeps)
-      for (uint32_t it = 0; !late && ((lo ^ tag) >> 32 || (hi ^ tag) >> 32); ++it) {
-        if (global_ns() - t0 > limit || it >= (1u << 26)) {
-          late = true;
-          break;
-        }
-        __nanosleep(64);
-        lo = ld_relaxed_sys(wp);
-        hi = ld_relaxed_sys(wp + 1);
+  for (int i = tid; i < R * E && !late; i += kDecodeThreads) {
+    const int r = i / E, e = i - r * E;
+    const unsigned long long* wp = own + kXchSlots + ((par * R + r) * E + e) * 2;
+    unsigned long long lo = ld_relaxed_sys(wp), hi = ld_relaxed_sys(wp + 1);
+    // time-bounded, and iteration-bounded too (at least ~4 s of 64 ns sleeps)
+    for (uint32_t it = 0; (lo ^ tag) >> 32 || (hi ^ tag) >> 32; ++it) {
+      if (global_ns() - t0 > limit || it >= (1u << 26)) {
+        late = true;
+        break;
       }
-      acc += (hi << 32) | (lo & 0xFFFFFFFFull);
+      __nanosleep(64);
+      lo = ld_relaxed_sys(wp);
+      hi = ld_relaxed_sys(wp + 1);
     }
-    // staged in hist (free between phases 1 and 2) so that sm.imp changes only if every
-    // rank's vector arrived
-    if (!late) sm.hist[e] = static_cast<long long>(acc);
+    if (!late)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&sm.hist[e]), (hi << 32) | (lo & 0xFFFFFFFFull));
   }
   if (late) atomicExch(&s_late, 1);
   __syncthreads();
