@@ -67,8 +67,8 @@ __device__ __forceinline__ void argmin_merge(float& v, int& pos, float ov, int o
   }
 }
 
-template <typename WT, typename IT, bool ALIGN>
-__device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm);
+template <typename WT, typename IT>
+__device__ void merge_routes(const DecodeParams& p);
 
 // ---- peer exchange: self-validating 8-byte words (see kXchSlots) ------------------------------
 __device__ __forceinline__ void st_relaxed_sys(unsigned long long* ptr, unsigned long long v) {
@@ -149,7 +149,7 @@ __device__ void exchange_importance(const DecodeParams& p, DecodeSmem& sm) {
   __syncthreads();
 }
 
-template <typename WT, typename IT, bool ALIGN = false>
+template <typename WT, typename IT, bool MERGE = false>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeParams p) {
   __shared__ DecodeSmem sm;
   const int E = p.experts;
@@ -362,37 +362,25 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
       }
     }
   }
-  if constexpr (ALIGN) merge_and_align<WT, IT, ALIGN>(p, sm);
+  if constexpr (MERGE) merge_routes<WT, IT>(p);
 }
 
-// ---- 5. (decode + moe_align) the expert layer's routing, from the routes phase 4 wrote -------
-// a. Routes of one token that the table sent to the same expert become one route: the first
-//    keeps the sum of their weights (fp32, slot order), the others get id -1 (so the expert
-//    layer computes that expert once for the token).  Out-of-range ids also get -1.
-// b. Each warp owns a contiguous range of routes and counts its routes per expert
-//    (__match_any_sync groups a step's 32 routes by expert), into a [32][E] uint16 table.
-// c. Exclusive prefix of the table over warps, per-expert totals, and the expert offsets (totals
-//    padded to 128-row blocks, scanned by one warp).
-// d. Padding entries (the route count) and the block -> expert map.
-// e. Each warp walks its range again in the same order and places route r at offset[e] +
-//    (routes of e in earlier warps) + (earlier routes of e in this warp): route order within an
-//    expert, as moe_align gives it.
+// ---- 5. (decode for the expert layer) the layer's routes, from the routes phase 4 wrote ------
+// Routes of one token that the table sent to the same expert become one route: the first keeps
+// the sum of their weights (fp32, slot order), the others get id -1 (so the expert layer computes
+// that expert once for the token).  Out-of-range ids also get -1.  moe_align and the gather of
+// token rows then run over these routes in one multi-CTA launch (align_gather_kernel).
 // Phase 4's writes are read back through L1 after the barrier (same CTA), never through the
 // read-only path.
-template <typename WT, typename IT, bool ALIGN>
-__device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm) {
-  const int kBlock = p.align_block > 0 ? p.align_block : 128;
+template <typename WT, typename IT>
+__device__ void merge_routes(const DecodeParams& p) {
   const int E = p.experts;
   const int K = p.top_k;
   const int R = static_cast<int>(p.routes);
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
   const WT* ow = static_cast<const WT*>(p.out_w);
   const IT* oi = static_cast<const IT*>(p.out_ids);
   __syncthreads();
-  // -- a
-  for (int t = tid; t < R / K; t += kDecodeThreads) {
+  for (int t = threadIdx.x; t < R / K; t += kDecodeThreads) {
     int e[8];
     float g[8];
 #pragma unroll
@@ -426,75 +414,6 @@ __device__ void merge_and_align(const DecodeParams& p, DecodeSmem& sm) {
         p.gemm_ids[t * K + j] = e[j];
         p.gemm_w[t * K + j] = g[j];
       }
-  }
-  // -- b
-  uint16_t* cnt = reinterpret_cast<uint16_t*>(sm.hist);  // [32][E], E <= 256: 16 KB
-  int* offs = reinterpret_cast<int*>(sm.imp);            // [E + 1]
-  int* total = offs + 512;                                // [E]
-  for (int i = tid; i < 32 * E; i += kDecodeThreads) cnt[i] = 0;
-  __syncthreads();
-  const int chunk = (R + 31) / 32;
-  const int r0 = warp * chunk;
-  const int r1 = r0 + chunk < R ? r0 + chunk : R;
-  for (int base = r0; base < r1; base += 32) {
-    const int r = base + lane;
-    const int e = r < r1 ? p.gemm_ids[r] : -1;
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && lane == __ffs(m) - 1) cnt[warp * E + e] += static_cast<uint16_t>(__popc(m));
-  }
-  __syncthreads();
-  // -- c
-  for (int e = tid; e < E; e += kDecodeThreads) {
-    int run = 0;
-    for (int w2 = 0; w2 < 32; ++w2) {
-      const int c = cnt[w2 * E + e];
-      cnt[w2 * E + e] = static_cast<uint16_t>(run);
-      run += c;
-    }
-    total[e] = run;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const int per = (E + 31) / 32;
-    int local = 0;
-    for (int i = 0; i < per; ++i) {
-      const int e = lane * per + i;
-      if (e < E) local += (total[e] + kBlock - 1) / kBlock * kBlock;
-    }
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    int run = incl - local;
-    for (int i = 0; i < per; ++i) {
-      const int e = lane * per + i;
-      if (e < E) {
-        offs[e] = run;
-        run += (total[e] + kBlock - 1) / kBlock * kBlock;
-      }
-    }
-    if (lane == 31) {
-      offs[E] = incl;
-      *p.num_post_pad = incl;
-    }
-  }
-  __syncthreads();
-  // -- d
-  for (int e = tid; e < E; e += kDecodeThreads) {
-    for (int i = offs[e] + total[e]; i < offs[e + 1]; ++i) p.sorted_ids[i] = R;
-    for (int b = offs[e] / kBlock; b < offs[e + 1] / kBlock; ++b) p.block_experts[b] = e;
-  }
-  // -- e
-  for (int base = r0; base < r1; base += 32) {
-    const int r = base + lane;
-    const int e = r < r1 ? p.gemm_ids[r] : -1;
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    if (e >= 0) p.sorted_ids[offs[e] + cnt[warp * E + e] + __popc(m & ((1u << lane) - 1u))] = r;
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(m) - 1) cnt[warp * E + e] += static_cast<uint16_t>(__popc(m));
-    __syncwarp();
   }
 }
 
@@ -591,7 +510,7 @@ __global__ void __launch_bounds__(256) static_remap_kernel(void* wv, void* idv, 
 }
 
 // ---------------------------------------------------------------------------------------------
-template <typename WT, typename IT, bool ALIGN = false>
+template <typename WT, typename IT, bool MERGE = false>
 static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
@@ -602,11 +521,11 @@ static cudaError_t launch_decode_t(const DecodeParams& p, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<WT, IT, ALIGN>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<WT, IT, MERGE>, p);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-cudaError_t launch_decode_align(const DecodeParams& p, cudaStream_t s) {
+cudaError_t launch_decode_merge(const DecodeParams& p, cudaStream_t s) {
   return launch_decode_t<float, int32_t, true>(p, s);
 }
 

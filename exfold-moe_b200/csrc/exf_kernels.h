@@ -83,15 +83,11 @@ struct DecodeParams {
   void* out_w;
   void* out_ids;
   int32_t* out_subset;
-  // decode + moe_align in the same launch (launch_decode_align only): the routes that the table
-  // sent to one expert twice in a token become one route, and moe_align runs over the result
+  // decode for the expert layer (launch_decode_merge only): the routes that the table sent to
+  // one expert twice in a token become one route
   int top_k;
   float* gemm_w;            // [routes] weights for the expert layer (merged in slot order)
   int32_t* gemm_ids;        // [routes] expert of each route; -1 for a merged or invalid route
-  int32_t* sorted_ids;      // moe_align outputs over gemm_ids, align_block-route blocks
-  int32_t* block_experts;
-  int32_t* num_post_pad;
-  int align_block;          // moe_align block size of the fused path (0: 128)
   // kImportanceExchanged only: this process's mapping of every rank's exchange buffer
   int world;
   int rank;
@@ -128,11 +124,12 @@ bool router_biased_eligible(int experts, int scoring, int fold, const RouterPara
 cudaError_t launch_router_biased(int fold, const RouterParams& p, cudaStream_t s);
 cudaError_t launch_fold(int w_dtype, int id_dtype, int variant, const FoldParams& p, cudaStream_t s);
 cudaError_t launch_decode(int w_dtype, int id_dtype, const DecodeParams& p, cudaStream_t s);
-// fp32 weights, int32 ids, experts <= kDecodeAlignMaxExperts, routes <= kDecodeAlignMaxRoutes,
-// top_k <= 8
+// Decode with the merged routes of the expert layer: fp32 weights, int32 ids, experts <=
+// kDecodeAlignMaxExperts, routes <= kDecodeAlignMaxRoutes (moe_align and the gather of the layer
+// then run in one align_gather launch), top_k <= 8
 constexpr int kDecodeAlignMaxExperts = 256;
 constexpr int kDecodeAlignMaxRoutes = 8192;
-cudaError_t launch_decode_align(const DecodeParams& p, cudaStream_t s);
+cudaError_t launch_decode_merge(const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_importance(int w_dtype, int id_dtype, const void* w, const void* ids,
                               int64_t routes, int experts, const float* norms, int64_t* imp,
                               cudaStream_t s);

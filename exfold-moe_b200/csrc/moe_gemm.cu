@@ -932,17 +932,20 @@ cudaError_t launch_decode_moe_experts(DecodeParams d, const MoeArgs& a, void* wo
   d.top_k = a.top_k;
   d.gemm_w = reinterpret_cast<float*>(extra);
   d.gemm_ids = reinterpret_cast<int32_t*>(extra + up256(a.tokens * a.top_k * 4));
-  d.sorted_ids = w.sorted_ids;
-  d.block_experts = w.expert_ids;
-  d.num_post_pad = w.num_post_pad;
-  d.align_block = gemm_block(a.tokens * a.top_k, a.experts);
-  // 1. decode and moe_align in one launch (the merged routes)
-  cudaError_t e = launch_decode_align(d, s);
+  // 1. decode, with the routes of one token to one expert merged
+  cudaError_t e = launch_decode_merge(d, s);
   if (e != cudaSuccess) return e;
+  // 2. moe_align over the merged routes and the gather of token rows, one launch
+  const int64_t numel = a.tokens * a.top_k;
+  AlignParams ap{d.gemm_ids, numel, a.experts, gemm_block(numel, a.experts), w.capacity,
+                 w.sorted_ids, w.expert_ids, w.num_post_pad, static_cast<int32_t*>(w.align_ws), 0};
+  e = launch_align_gather(ap, a.x, a.top_k, a.hidden, w.xs, w.layer_sync, w.layer_sync_ints, s);
+  if (e != cudaSuccess) return e;
+  // 3. the expert layer over the merged routes
   MoeArgs m = a;
   m.topk_w = d.gemm_w;
   m.topk_ids = d.gemm_ids;
-  return launch_moe_compute(m, w, s);
+  return launch_moe_gemms(m, w, s);
 }
 
 }  // namespace exf

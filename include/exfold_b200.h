@@ -223,13 +223,13 @@ EXF_API int exf_fused_experts(const void* x, const float* topk_w, const int32_t*
                               int experts, int hidden, int inter, void* y, void* workspace,
                               int64_t workspace_bytes, int32_t* status, exf_stream_t stream);
 
-/* Decode expert budget followed by the expert layer, with the routing between them fused into
- * the decode launch: select_and_reroute_decode / exfold_decode_cuda
- * (exfold/qwen3/kernels.py:423-491; exfold_kernels.cu:280-322), then vLLM moe_align_block_size
- * (moe_align_block_size.py:11-93) and fused_experts (fused_moe.py:1587) over the remapped routes.
- * The decode launch also merges the routes of a token that the table sent to the same expert
- * (their weights summed in slot order, the expert computed once) and writes the moe_align
- * outputs for the merged routes, so the layer is that launch plus gather, two GEMMs and combine.
+/* Decode expert budget followed by the expert layer: select_and_reroute_decode /
+ * exfold_decode_cuda (exfold/qwen3/kernels.py:423-491; exfold_kernels.cu:280-322), then vLLM
+ * moe_align_block_size (moe_align_block_size.py:11-93) and fused_experts (fused_moe.py:1587)
+ * over the remapped routes.  The decode launch also merges the routes of a token that the table
+ * sent to the same expert (their weights summed in slot order, the expert computed once); the
+ * layer is then one launch for moe_align and the gather of token rows, one for both GEMMs and
+ * one for the combine.
  * out_w / out_ids [batch][top_k] receive exf_decode's outputs bit for bit; y bf16
  * [batch][hidden] equals exf_fused_experts over them within bf16 rounding (a merged route's
  * output is rounded once instead of twice).  w fp32, ids int32; experts <= 256, top_k <= 8,
