@@ -338,11 +338,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
         sm.cterm[e] = __fadd_rn(0.5f, b);
       }
       if (FOLD != kFoldNone) {
+        // 16 loads in flight per thread before their stores: the 256 KB table costs 4 L2 (or,
+        // after L2 was flushed, DRAM) round trips instead of one per few 16-byte vectors
+        constexpr int kBatch = 16;
+        constexpr int kStride = kWarps * 32;
+        static_assert((kE * kE / 4) % (kBatch * kStride) == 0, "loss table copy batches");
         const uint4* src = reinterpret_cast<const uint4*>(p.sel_loss + l * kE * kE);
         uint2* dst = reinterpret_cast<uint2*>(sm.loss_hi);
-        for (int i = threadIdx.x; i < kE * kE / 4; i += kWarps * 32) {
-          const uint4 v = __ldg(src + i);
-          dst[i] = make_uint2(__byte_perm(v.x, v.y, 0x7632), __byte_perm(v.z, v.w, 0x7632));
+        for (int i0 = threadIdx.x; i0 < kE * kE / 4; i0 += kBatch * kStride) {
+          uint4 v[kBatch];
+#pragma unroll
+          for (int b = 0; b < kBatch; ++b) v[b] = __ldg(src + i0 + b * kStride);
+#pragma unroll
+          for (int b = 0; b < kBatch; ++b)
+            dst[i0 + b * kStride] = make_uint2(__byte_perm(v[b].x, v[b].y, 0x7632),
+                                               __byte_perm(v[b].z, v[b].w, 0x7632));
         }
       }
     }
