@@ -437,6 +437,48 @@ def _expert_weights(experts, hidden, inter, seed, dev):
     return w13, w2
 
 
+def _gpu_local_cpus(dev):
+    """The CPUs of the GPU's NUMA node (sysfs local_cpulist), within this process's affinity;
+    None when unknown."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        bdf = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        with open(f"/sys/bus/pci/devices/{bdf}/local_cpulist") as f:
+            text = f.read().strip()
+        cpus = set()
+        for part in text.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None
+
+
+class near_gpu:
+    """Pinned host buffers allocated inside this block get their pages on the GPU's NUMA node
+    (the calling thread runs there while they are allocated and first written); the process's
+    CPU affinity is restored on exit, so later CPU work still uses every core."""
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.saved = None
+
+    def __enter__(self):
+        cpus = _gpu_local_cpus(self.dev)
+        if cpus is not None:
+            self.saved = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+        return False
+
+
 def _hbm(nbytes, ms, peaks):
     gbs = nbytes / ms / 1e6
     return {"bytes": int(nbytes), "gbs": gbs, "frac": gbs / peaks["hbm_gbs"]}
@@ -785,10 +827,13 @@ def run_ours(args) -> None:
 
         # end to end through the public API: pinned host logits in, pinned host results out
         slots = min(4, LAYERS)
-        host_in = torch.empty((slots, TOKENS, EXPERTS), dtype=torch.float32).pin_memory()
-        host_in.copy_(logits[:slots].cpu())
-        host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
-        host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
+        with near_gpu(dev):  # host pages on the GPU's NUMA node: the copies stay on its socket
+            host_in = torch.empty((slots, TOKENS, EXPERTS), dtype=torch.float32).pin_memory()
+            host_in.copy_(logits[:slots].cpu())
+            host_w = torch.empty((slots, TOKENS, KEEP), dtype=torch.float32).pin_memory()
+            host_i = torch.empty((slots, TOKENS, KEEP), dtype=torch.int32).pin_memory()
+            host_w.zero_()
+            host_i.zero_()
         dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.float32, device=dev)
         dev_w = torch.empty((2, TOKENS, KEEP), dtype=torch.float32, device=dev)
         dev_i = torch.empty((2, TOKENS, KEEP), dtype=torch.int32, device=dev)
@@ -864,7 +909,8 @@ def run_ours(args) -> None:
         h2d = LAYERS * TOKENS * EXPERTS * 4
         d2h = LAYERS * TOKENS * KEEP * 8
         # the same with bf16 logits on the host (the served gate output dtype): half the H2D bytes
-        host_in = host_in.to(torch.bfloat16).pin_memory()
+        with near_gpu(dev):
+            host_in = host_in.to(torch.bfloat16).pin_memory()
         dev_in = torch.empty((2, TOKENS, EXPERTS), dtype=torch.bfloat16, device=dev)
         with torch.cuda.stream(stream):
             ms_e2e16 = timed(e2e_step, e2e_steps) / e2e_steps
