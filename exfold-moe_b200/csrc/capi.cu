@@ -82,7 +82,9 @@ static bool good_idtype(int d) { return d == EXF_I32 || d == EXF_I64; }
 // ---- entry points ---------------------------------------------------------------------------
 extern "C" {
 
-EXF_API int exf_abi_version(void) { return 2; }
+EXF_API int exf_abi_version(void) { return 3; }
+
+EXF_API int64_t exf_router_tile_min_rows(int64_t rows) { return router_tile_min_rows(rows); }
 
 EXF_API const char* exf_last_error(void) { return g_err; }
 

@@ -110,6 +110,9 @@ struct AlignParams {
 };
 
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p, cudaStream_t s);
+// Rows (tokens x layers) from which launch_router takes the tile kernels; sets it when rows >= 0
+// and returns the previous value.
+int64_t router_tile_min_rows(int64_t rows);
 cudaError_t launch_router_hash(const void* logits, int logit_dtype, int64_t tokens, int experts,
                                int top_k, int scoring, const void* token_ids, int id_dtype,
                                const int32_t* table, int64_t table_rows, int renormalize,

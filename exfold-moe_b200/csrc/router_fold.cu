@@ -19,6 +19,8 @@
 //   reference-compatible API that receives (weights, ids).
 #include <float.h>
 
+#include <atomic>
+
 #include "exf_common.cuh"
 #include "exf_kernels.h"
 #include "exf_launch.h"
@@ -734,10 +736,26 @@ static cudaError_t launch_router_s(int experts, const RouterParams& p, cudaStrea
   }
 }
 
+// The tile kernels keep a CTA per SM streaming 32- or 16-token tiles; a launch below about
+// 32768 rows gives each warp at most one tile, and the generic kernel's shorter per-token chain
+// then finishes first (L2 flushed, us per launch, tile / generic: E = 128 softmax + fold at 4096
+// rows 12.3 / 10.2, 16384 rows 14.3 / 14.3, 65536 rows 22.5 / 26.6; E = 256 biased sigmoid +
+// DeepSeek fold 22.5 / 12.3, 24.6 / 20.6, 49.2 / 55.3; without a fold 16.4 / 12.3 at 4096 and
+// 40.9 / 38.9 at 65536 rows).
+static std::atomic<int64_t> g_tile_min_rows{32768};
+
+int64_t router_tile_min_rows(int64_t rows) {
+  return rows >= 0 ? g_tile_min_rows.exchange(rows) : g_tile_min_rows.load();
+}
+
 cudaError_t launch_router(int experts, int scoring, int fold, const RouterParams& p,
                           cudaStream_t stream) {
-  if (router_tpt_eligible(experts, scoring, fold, p)) return launch_router_tpt(fold, p, stream);
-  if (router_biased_eligible(experts, scoring, fold, p))
+  const int64_t rows = p.tokens * p.layers;
+  const int64_t min_rows = g_tile_min_rows.load(std::memory_order_relaxed);
+  if (rows >= min_rows && router_tpt_eligible(experts, scoring, fold, p))
+    return launch_router_tpt(fold, p, stream);
+  if (rows >= (fold == kFoldNone ? 4 * min_rows : min_rows) &&
+      router_biased_eligible(experts, scoring, fold, p))
     return launch_router_biased(fold, p, stream);
   if (scoring == EXF_SOFTMAX) {
     if (fold == kFoldNone) return launch_router_s<EXF_SOFTMAX, kFoldNone>(experts, p, stream);

@@ -26,6 +26,7 @@ _vp, _i, _i64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_floa
 SIGNATURES = {
     "exf_abi_version": (_i, []),
     "exf_last_error": (ctypes.c_char_p, []),
+    "exf_router_tile_min_rows": (_i64, [_i64]),
     "exf_router_topk": (_i, [_vp, _i, _i64, _i, _i, _i, _vp, _i, _f, _vp, _vp, _vp]),
     "exf_router_fold_prefill": (_i, [_vp, _i, _i64, _i, _i, _i, _i, _vp, _i, _f, _i, _i, _i, _vp,
                                      _vp, _vp, _vp, _vp, _vp]),

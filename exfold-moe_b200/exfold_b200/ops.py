@@ -146,6 +146,13 @@ def router_fold_prefill(logits: torch.Tensor, top_k: int, target_k: int, coeff: 
 
 
 # ---- prefill fold of given routes -------------------------------------------------------------
+def router_tile_min_rows(rows: int | None = None) -> int:
+    """The launch size (tokens x layers) from which the router calls use the tile kernels
+    (exf_router_tile_min_rows): smaller launches take the generic kernel, whose latency is lower
+    there; both give identical results.  Sets it when `rows` is given; returns the previous value."""
+    return int(L.lib().exf_router_tile_min_rows(-1 if rows is None else int(rows)))
+
+
 def fold_prefill(weights: torch.Tensor, ids: torch.Tensor, coeff: torch.Tensor,
                  sel_loss: torch.Tensor, target_k: int, *, variant: str = "qwen3",
                  renorm_mode: int = 0, conf_loss: torch.Tensor | None = None,

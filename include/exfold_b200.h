@@ -59,6 +59,14 @@ enum exf_renorm { EXF_RENORM_NONE = 0, EXF_RENORM_ROUTER_L2 = 1, EXF_RENORM_SIMI
 EXF_API int exf_abi_version(void);
 EXF_API const char* exf_last_error(void);
 
+/* Router kernel choice.  The tile kernels (one token per lane over bulk-copied logit tiles, for
+ * E = 128 softmax and E = 256 biased sigmoid) are the fastest on large launches; below
+ * `rows` = tokens x layers (default 32768; 4x that for the biased kernel without a fold) the
+ * generic kernel (a token per E/32 lanes) has the lower latency.  Both give identical results.
+ * Sets the threshold for every later call in the process and returns the previous one; a
+ * negative `rows` only returns it. */
+EXF_API int64_t exf_router_tile_min_rows(int64_t rows);
+
 /* Router scoring + top-k.  Replaces vLLM fused_topk (softmax; exfold/qwen3/vllm_patch.py:98-109)
  * and fused_topk_bias (sigmoid or sqrtsoftplus + selection bias; exfold/deepseek_v4/
  * vllm_patch.py:175-209).  logits [tokens][experts] of logit_dtype (EXF_F32, EXF_BF16 or EXF_F16:

@@ -28,7 +28,23 @@ def test_library_loads_and_exports_header_symbols():
         assert hasattr(lib, name), name
         assert name in L.SIGNATURES, f"{name} has no ctypes signature"
     assert set(L.SIGNATURES) == set(names)
-    assert lib.exf_abi_version() == 2
+    assert lib.exf_abi_version() == 3
+
+
+def test_router_tile_threshold_knob():
+    """exf_router_tile_min_rows sets the launch size from which the tile router kernels are
+    taken and returns the previous value; a negative argument only reads it."""
+    lib = L.lib()
+    default = lib.exf_router_tile_min_rows(-1)
+    assert default == 32768
+    try:
+        assert lib.exf_router_tile_min_rows(0) == default
+        assert lib.exf_router_tile_min_rows(-1) == 0
+        assert lib.exf_router_tile_min_rows(1 << 40) == 0
+        assert lib.exf_router_tile_min_rows(-5) == 1 << 40
+    finally:
+        lib.exf_router_tile_min_rows(default)
+    assert lib.exf_router_tile_min_rows(-1) == default
 
 
 def test_capacity_matches_vllm_rule():

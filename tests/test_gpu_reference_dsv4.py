@@ -24,7 +24,7 @@ from exfold_b200 import ops
 from exfold_b200 import workloads as W
 from oracle import build_ref
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("router_kernel_choice")]
 DEV = torch.device("cuda:0")
 
 

@@ -15,7 +15,7 @@ from exfold_b200 import ops
 from exfold_b200 import workloads as W
 from oracle import oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("router_kernel_choice")]
 DEV = torch.device("cuda:0")
 E = 256
 

@@ -14,7 +14,7 @@ from exfold_b200 import workloads as W
 from exfold_b200.qwen3.router import make_router
 from oracle import oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("router_kernel_choice")]
 DEV = torch.device("cuda:0")
 
 
