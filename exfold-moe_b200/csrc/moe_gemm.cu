@@ -2,7 +2,8 @@
 //
 // After moe_align, routes are grouped by expert and padded to blocks (128 routes at prefill, 64 at
 // decode).  Per MoE layer:
-//   gather : xs[m] = x[token(sorted_ids[m])]                      (bf16 rows of real routes)
+//   gather : xs[m] = x[token(sorted_ids[m])] (bf16 rows of real routes; at <= 8192 routes done
+//            inside the moe_align launch, align_gather_kernel in moe_align.cu)
 //   GEMM-1 : act[m, n] = silu(xs[m] . W1[e, n]) * (xs[m] . W3[e, n]) for n in a 128-wide tile;
 //            gate and up rows of W13[e] are stacked into one N = 256 MMA so both accumulators
 //            sit side by side in TMEM and the SwiGLU epilogue needs no second pass
