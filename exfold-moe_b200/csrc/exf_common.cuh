@@ -62,6 +62,25 @@ __device__ __forceinline__ float exact_exp(float x) {
   return __fmul_rn(p, __int_as_float((ni + 127) << 23));
 }
 
+// exact_exp for arguments that are never above 88 (differences from a row maximum, or NaN):
+// the same operations without the upper clamp, so the same bits.
+__device__ __forceinline__ float exact_exp_le88(float x) {
+  x = (x > -87.0f) ? x : -87.0f;
+  const float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fmaf_rn(n, -kLn2Hi, x);
+  r = __fmaf_rn(n, -kLn2Lo, r);
+  float p = 0x1.a01a02p-13f;
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);
+  p = __fmaf_rn(p, r, 0x1p-1f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = __float2int_rz(n);
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
 __device__ __forceinline__ float exact_sigmoid(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, exact_exp(-x)));
 }

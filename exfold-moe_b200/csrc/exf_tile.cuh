@@ -55,8 +55,24 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
+// three-input max (PTX 8.8, sm_100): NaN when any input is NaN / the largest non-NaN input
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ void cx32(uint32_t& a, uint32_t& b) {
   const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+__device__ __forceinline__ void cxs32(int32_t& a, int32_t& b) {
+  const int32_t hi = max(a, b), lo = min(a, b);
   a = hi;
   b = lo;
 }
@@ -87,6 +103,17 @@ __device__ __forceinline__ void merge8(uint32_t* a, const uint32_t* b, uint32_t&
   cx32(a[0], a[4]); cx32(a[1], a[5]); cx32(a[2], a[6]); cx32(a[3], a[7]);
   cx32(a[0], a[2]); cx32(a[1], a[3]); cx32(a[4], a[6]); cx32(a[5], a[7]);
   cx32(a[0], a[1]); cx32(a[2], a[3]); cx32(a[4], a[5]); cx32(a[6], a[7]);
+}
+// merge8 on signed keys
+__device__ __forceinline__ void merge8s(int32_t* a, const int32_t* b, int32_t& dmax) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    dmax = max(dmax, min(a[i], b[7 - i]));
+    a[i] = max(a[i], b[7 - i]);
+  }
+  cxs32(a[0], a[4]); cxs32(a[1], a[5]); cxs32(a[2], a[6]); cxs32(a[3], a[7]);
+  cxs32(a[0], a[2]); cxs32(a[1], a[3]); cxs32(a[4], a[6]); cxs32(a[5], a[7]);
+  cxs32(a[0], a[1]); cxs32(a[2], a[3]); cxs32(a[4], a[5]); cxs32(a[6], a[7]);
 }
 // Insert v into T (sorted descending), dropping the smallest.
 __device__ __forceinline__ void insert8(uint64_t (&T)[8], uint64_t v) {

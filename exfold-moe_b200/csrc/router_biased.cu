@@ -21,8 +21,9 @@
 //     sigmoid on B200 (exhaustive sweep) and exact_sigmoid within 9e-8, so |a~ - exact score|
 //     <= kErrAbs + kErrRel |score| with a factor-2 margin (the roundings of the bias terms are
 //     the relative part).
-//   * Each lane keys its 32 group maxima (groups of 4 columns; low 6 bits of the key name the
-//     group) and sorts them (4 x 19-comparator networks, 3 merges); one merge with the partner
+//   * Each lane keys its 32 group maxima (groups of 4 columns, maxima by three-input max; the
+//     key is the maximum's raw bits as a signed integer with the low 6 bits naming the group)
+//     and sorts them (4 x 19-comparator networks, 3 merges); one merge with the partner
 //     lane gives the token's 8 groups with the largest approximate maxima and the 9th largest.
 //     The token's lane re-scores those 8 groups from global memory (L2; the slot is already
 //     refilled) and keys each group's maximum exactly (exact_sigmoid + bias).  With A8 the
@@ -112,18 +113,24 @@ constexpr uint32_t kFltMaxHi = 0x7F7F0000u;
 
 // merge8 (exf_tile.cuh) that keeps the two largest values dropped so far: d1 >= d2 (over a whole
 // merge tree: the 9th and 10th largest inputs)
-__device__ __forceinline__ void merge8_2(uint32_t* a, const uint32_t* b, uint32_t& d1,
-                                         uint32_t& d2) {
+__device__ __forceinline__ void merge8_2(int32_t* a, const int32_t* b, int32_t& d1,
+                                         int32_t& d2) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t lo = min(a[i], b[7 - i]);
+    const int32_t lo = min(a[i], b[7 - i]);
     a[i] = max(a[i], b[7 - i]);
     d2 = max(d2, min(d1, lo));
     d1 = max(d1, lo);
   }
-  cx32(a[0], a[4]); cx32(a[1], a[5]); cx32(a[2], a[6]); cx32(a[3], a[7]);
-  cx32(a[0], a[2]); cx32(a[1], a[3]); cx32(a[4], a[6]); cx32(a[5], a[7]);
-  cx32(a[0], a[1]); cx32(a[2], a[3]); cx32(a[4], a[5]); cx32(a[6], a[7]);
+  cxs32(a[0], a[4]); cxs32(a[1], a[5]); cxs32(a[2], a[6]); cxs32(a[3], a[7]);
+  cxs32(a[0], a[2]); cxs32(a[1], a[3]); cxs32(a[4], a[6]); cxs32(a[5], a[7]);
+  cxs32(a[0], a[1]); cxs32(a[2], a[3]); cxs32(a[4], a[5]); cxs32(a[6], a[7]);
+}
+
+// A truncated signed key (low 6 bits replaced) rounded up in value: low bits set for a positive
+// float, cleared for a negative one.
+__device__ __forceinline__ float key_ceil(int32_t k) {
+  return __int_as_float(k >= 0 ? (k | 63) : (k & ~63));
 }
 
 // Sorted insertion of (packed key, sigmoid) into the descending list T / S, dropping the last.
@@ -249,8 +256,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
   // Group maxima of tile k for this lane's half of token r (lanes past the end of a short tile
   // use the tile's first token): pk = the token's 8 largest packed maxima, p9 the 9th.  Waits for
   // the tile's copy and refills the slot afterwards; false if a wait timed out.  Warp-uniform.
-  auto group_maxima = [&](int64_t k, int rowi, uint32_t (&pk)[kK], uint32_t& p9,
-                          uint32_t& p10) -> bool {
+  auto group_maxima = [&](int64_t k, int rowi, int32_t (&pk)[kK], int32_t& p9,
+                          int32_t& p10) -> bool {
     const int slot = static_cast<int>(k % kSlots);
     bool ok = !*failed;
     if (ok && t == 0) {
@@ -268,7 +275,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       *failed = 1;
     }
     // approximate group maxima, keyed: the only reads of the tile
-    uint32_t g[32];
+    int32_t g[32];
     if (ok) {
       const LT* rowp = sm.tile[slot] + rowi * kE;
 #pragma unroll
@@ -278,10 +285,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
           const int c = 32 * h + static_cast<int>(static_cast<uint32_t>(8 * s + i) ^ swz);
           const float4 v = load_logits4(rowp + 4 * c);
           const float4 cc = *reinterpret_cast<const float4*>(sm.cterm + 4 * c);
-          const float m = fmax_nan(fmax_nan(approx_biased(v.x, cc.x), approx_biased(v.y, cc.y)),
-                                   fmax_nan(approx_biased(v.z, cc.z), approx_biased(v.w, cc.w)));
+          const float m = fmax_nan(fmax3_nan(approx_biased(v.x, cc.x), approx_biased(v.y, cc.y),
+                                             approx_biased(v.z, cc.z)),
+                                   approx_biased(v.w, cc.w));
           const uint32_t id = (static_cast<uint32_t>(h) << 5) | (8 * s + i);
-          g[8 * s + i] = (order_key(m) & ~63u) | (63u - id);
+          g[8 * s + i] = static_cast<int32_t>((__float_as_uint(m) & ~63u) | (63u - id));
         }
     }
     // the tile is consumed: refill its slot with local tile k + kSlots before the sorting
@@ -294,24 +302,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       __threadfence_block();
       seq[slot] = k + kSlots;
     }
-    p9 = 0;
-    p10 = 0;
+    p9 = INT32_MIN;
+    p10 = INT32_MIN;
 #pragma unroll
-    for (int q = 0; q < kK; ++q) pk[q] = 0;
+    for (int q = 0; q < kK; ++q) pk[q] = INT32_MIN;
     if (ok) {
-      sort8<uint32_t, cx32>(g);
-      sort8<uint32_t, cx32>(g + 8);
-      sort8<uint32_t, cx32>(g + 16);
-      sort8<uint32_t, cx32>(g + 24);
+      sort8<int32_t, cxs32>(g);
+      sort8<int32_t, cxs32>(g + 8);
+      sort8<int32_t, cxs32>(g + 16);
+      sort8<int32_t, cxs32>(g + 24);
       merge8_2(g, g + 8, p9, p10);
       merge8_2(g + 16, g + 24, p9, p10);
       merge8_2(g, g + 16, p9, p10);
       // the partner lane's 8 groups: both lanes end with the same sorted top 8 of the token
-      uint32_t o[8];
+      int32_t o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xffffffffu, g[i], 1);
-      const uint32_t o9 = __shfl_xor_sync(0xffffffffu, p9, 1);
-      const uint32_t o10 = __shfl_xor_sync(0xffffffffu, p10, 1);
+      const int32_t o9 = __shfl_xor_sync(0xffffffffu, p9, 1);
+      const int32_t o10 = __shfl_xor_sync(0xffffffffu, p10, 1);
       merge8_2(g, o, p9, p10);
       // the partner's two largest dropped values
       p10 = max(p10, min(p9, o9));
@@ -378,11 +386,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       const bool use_b = h && has_b;
       // Tiles A and B in a loop that is not unrolled (one copy of the group-maxima code: the
       // kernel's instruction fetch was a top stall); each lane keeps its own tile's result.
-      uint32_t pk[kK] = {}, p9 = 0, p10 = 0;
+      int32_t pk[kK] = {}, p9 = INT32_MIN, p10 = INT32_MIN;
       bool ok = true;
 #pragma unroll 1
       for (int which = 0; which < (has_b ? 2 : 1); ++which) {
-        uint32_t tk[kK], t9 = 0, t10 = 0;
+        int32_t tk[kK], t9 = INT32_MIN, t10 = INT32_MIN;
         ok = group_maxima(ks + j + which, which ? rb : ra, tk, t9, t10) && ok;
         if (which == (use_b ? 1 : 0)) {
 #pragma unroll
@@ -444,9 +452,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       if (!sorted) sort8p(T, S);
       const float a8 = float_of_key(static_cast<uint32_t>(T[kK - 1] >> 32));
       const float bound = __fsub_rn(a8, __fmaf_rn(kErrRel, fabsf(a8), kErrAbs));
-      const float g9 = float_of_key((p9 & ~63u) | 63u);
-      const float g10 = float_of_key((p10 & ~63u) | 63u);
-      const bool nonfinite = (pk[0] & ~63u) >= 0xFF800000u;  // +inf or NaN approximate maximum
+      // The 9th and 10th largest approximate maxima rounded up.  Keys are the raw bits of the
+      // maxima compared as signed integers, so negative maxima rank in reverse among themselves:
+      // when a negative maximum is named, every other negative one is larger and the test below
+      // fails (the exact path ranks the row); when the 9th or 10th is negative, every negative
+      // maximum is below the positive bound.
+      const float g9 = key_ceil(p9);
+      const float g10 = key_ceil(p10);
+      const bool nonfinite = (pk[0] & ~63) >= 0x7F800000;  // +inf or NaN approximate maximum
       if (!nonfinite && g10 < bound) {
         // every element outside the 8 groups and the 9th is below bound: insert the other
         // elements of the 8 groups that reach bound (their logits are in registers) ...

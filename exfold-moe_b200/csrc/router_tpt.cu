@@ -256,64 +256,69 @@ __global__ void __launch_bounds__(tpt_warps<LT>() * 32, 1) router_tpt_kernel(con
         // keeps its high 27 bits; the low 5 hold 31 - u (fp32: a constant per step) or, for
         // 16-bit logits, 31 - group, so that equal keys sort by ascending group, i.e. ascending
         // column.
+        // Keys are the raw bits of the float maxima compared as signed integers: positive floats
+        // (and +inf, and the canonical NaN that max.NaN returns, above +inf) rank by value above
+        // every negative one; negative floats rank in reverse among themselves, which only the
+        // exact path sees (the fast path needs a positive 8th maximum).
         constexpr bool kExactKeys = sizeof(LT) == 2;
-        uint32_t pk[32];
+        int32_t pk[32];
 #pragma unroll
         for (int s = 0; s < 4; ++s)
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t grp = static_cast<uint32_t>((8 * s + i) ^ swz);
             const float4 v = load_logits4(rowp + 4 * grp);
-            const uint32_t g = order_key(fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
-            pk[8 * s + i] = (g & ~31u) | (31u - (kExactKeys ? grp : 8 * s + i));
+            const float m = fmax_nan(fmax3_nan(v.x, v.y, v.z), v.w);
+            pk[8 * s + i] = static_cast<int32_t>((__float_as_uint(m) & ~31u) |
+                                                 (31u - (kExactKeys ? grp : 8 * s + i)));
           }
-        sort8<uint32_t, cx32>(pk);
-        sort8<uint32_t, cx32>(pk + 8);
-        sort8<uint32_t, cx32>(pk + 16);
-        sort8<uint32_t, cx32>(pk + 24);
-        uint32_t p9 = 0;  // the 9th largest packed maximum
-        merge8(pk, pk + 8, p9);
-        merge8(pk + 16, pk + 24, p9);
-        merge8(pk, pk + 16, p9);
+        sort8<int32_t, cxs32>(pk);
+        sort8<int32_t, cxs32>(pk + 8);
+        sort8<int32_t, cxs32>(pk + 16);
+        sort8<int32_t, cxs32>(pk + 24);
+        int32_t p9 = INT32_MIN;  // the 9th largest packed maximum
+        merge8s(pk, pk + 8, p9);
+        merge8s(pk + 16, pk + 24, p9);
+        merge8s(pk, pk + 16, p9);
 
         // ---- the 8 named groups: exact maxima, sorted by (key desc, column asc) -------------
-        uint32_t ek[kK][4];
+        // A 16-bit logit converted to fp32 has its low 16 bits all zeros, so for 16-bit logits
+        // the truncated keys are exact: the named groups' maxima are in (value desc, column asc)
+        // order, and an element of any other group either is below the 8th maximum or equals it
+        // at a higher column, so it is not in the top 8.  fp32 keys lose their low 5 bits: the
+        // order holds when the truncated keys differ, and the other groups are excluded when the
+        // 9th truncated maximum is below the 8th.  The fast path needs the 8th truncated maximum
+        // positive (no zeros or negative values among the candidates) and no NaN in the row;
+        // the named maxima are then positive, their order keys are their bits with the sign bit
+        // set, and every comparison below is a float comparison of positive values.
+        const bool apart = kExactKeys || (p9 >> 5) < (pk[kK - 1] >> 5);
+        const bool nan_row = pk[0] > 0x7F80001F;  // above +inf: max.NaN found a NaN
+        const bool fast = apart && pk[kK - 1] >= 32 && !nan_row;
+        float4 xv[kK];
         int cb[kK], emax[kK];
 #pragma unroll
         for (int i = 0; i < kK; ++i) {
-          const uint32_t slot = 31u - (pk[i] & 31u);
+          const uint32_t slot = 31u - (static_cast<uint32_t>(pk[i]) & 31u);
           cb[i] = 4 * static_cast<int>(kExactKeys ? slot : slot ^ static_cast<uint32_t>(swz));
           const float4 v = load_logits4(rowp + cb[i]);
-          ek[i][0] = order_key(v.x);
-          ek[i][1] = order_key(v.y);
-          ek[i][2] = order_key(v.z);
-          ek[i][3] = order_key(v.w);
-          const uint32_t m = max(max(ek[i][0], ek[i][1]), max(ek[i][2], ek[i][3]));
-          emax[i] = ek[i][0] == m ? 0 : (ek[i][1] == m ? 1 : (ek[i][2] == m ? 2 : 3));
-          T[i] = pack(m, cb[i] + emax[i]);
+          xv[i] = v;
+          const float m = fmaxf(fmax3(v.x, v.y, v.z), v.w);
+          emax[i] = v.x == m ? 0 : (v.y == m ? 1 : (v.z == m ? 2 : 3));
+          T[i] = pack(__float_as_uint(m) | 0x80000000u, cb[i] + emax[i]);
         }
-        // A 16-bit logit converted to fp32 has its low 16 bits all zeros (its key all zeros or
-        // all ones there), so for 16-bit logits the truncated keys are exact: the named groups'
-        // maxima are in (key desc, column asc) order, and an element of any other group either
-        // is below the 8th maximum or equals it at a higher column, so it is not in the top 8.
-        // fp32 keys lose their low 5 bits: the order holds when the truncated keys differ, and
-        // the other groups are excluded when the 9th truncated maximum is below the 8th.
-        bool distinct = true;
         if (!kExactKeys) {
+          uint32_t dmin = 0xFFFFFFFFu;  // truncated keys differ where the xor reaches bit 5
 #pragma unroll
           for (int i = 0; i + 1 < kK; ++i)
-            distinct = distinct && (pk[i] >> 5) != (pk[i + 1] >> 5);
+            dmin = min(dmin, static_cast<uint32_t>(pk[i] ^ pk[i + 1]));
+          if (dmin < 32u) sort8<uint64_t, cx64>(T);
         }
-        if (!distinct) sort8<uint64_t, cx64>(T);
-        const uint32_t theta = static_cast<uint32_t>(T[kK - 1] >> 32);
-        const bool apart = kExactKeys || (p9 >> 5) < (pk[kK - 1] >> 5);
-        const bool nan_row = pk[0] >= 0xFFFFFFE0u;
-        const bool fast = apart && theta > kKeyPosZero && !nan_row;
 
         if (fast) {
           // other elements of the named groups that reach theta: a mask over the 32 (group,
           // element) sites, each inserted after a reload from the tile (typically 0-2 of them)
-          uint32_t xm = 0, slo = 0, shi = 0;
+          const float theta = __uint_as_float(static_cast<uint32_t>(T[kK - 1] >> 32) & 0x7FFFFFFFu);
+          uint32_t xm = 0, mm = 0, slo = 0, shi = 0;
 #pragma unroll
           for (int i = 0; i < kK; ++i) {
             const uint32_t grp = static_cast<uint32_t>(cb[i]) >> 2;
@@ -321,23 +326,28 @@ __global__ void __launch_bounds__(tpt_warps<LT>() * 32, 1) router_tpt_kernel(con
               slo |= grp << (5 * i);
             else
               shi |= grp << (5 * (i - 6));
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              xm |= (e != emax[i] && ek[i][e] >= theta ? 1u : 0u) << (4 * i + e);
+            xm |= (xv[i].x >= theta ? 1u : 0u) << (4 * i);
+            xm |= (xv[i].y >= theta ? 2u : 0u) << (4 * i);
+            xm |= (xv[i].z >= theta ? 4u : 0u) << (4 * i);
+            xm |= (xv[i].w >= theta ? 8u : 0u) << (4 * i);
+            mm |= 1u << (4 * i + emax[i]);
           }
+          xm &= ~mm;
           while (xm) {
             const int site = __ffs(xm) - 1;
             xm &= xm - 1;
             const int i = site >> 2;
             const uint32_t grp = (i < 6 ? slo >> (5 * i) : shi >> (5 * (i - 6))) & 31u;
             const int col = 4 * static_cast<int>(grp) + (site & 3);
-            insert8(T, pack(order_key(logit_f32<LT>(rowp[col])), col));
+            insert8(T, pack(__float_as_uint(logit_f32<LT>(rowp[col])) | 0x80000000u, col));
           }
         } else if (valid) {
-          // exact insertion over every element of every group whose maximum reaches the bound
-          // (pk[7] truncated is below the 8th largest key); a row with a NaN inserts every element
+          // exact insertion over every element of every group whose maximum reaches the bound:
+          // the 8th truncated maximum rounded down in value (a row with a NaN: every element)
+          const uint32_t b8 = static_cast<uint32_t>(pk[kK - 1]);
+          const uint32_t lb = pk[kK - 1] >= 0 ? (b8 & ~31u) | 0x80000000u : ~(b8 | 31u);
           uint64_t Te[kK];
-          exact_top8<LT>(rowp, swz, nan_row ? 0u : pk[kK - 1] & ~31u, Te);
+          exact_top8<LT>(rowp, swz, nan_row ? 0u : lb, Te);
 #pragma unroll
           for (int q = 0; q < kK; ++q) T[q] = Te[q];
         }
@@ -392,7 +402,7 @@ __global__ void __launch_bounds__(tpt_warps<LT>() * 32, 1) router_tpt_kernel(con
           float norm = 0.0f;
 #pragma unroll
           for (int s = 0; s < kK; ++s) {
-            w[s] = exact_exp(__fsub_rn(val[s], val[0]));
+            w[s] = exact_exp_le88(__fsub_rn(val[s], val[0]));  // val[s] <= val[0], or NaN
             norm = __fadd_rn(norm, w[s]);
           }
 #pragma unroll
