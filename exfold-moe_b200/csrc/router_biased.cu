@@ -25,18 +25,20 @@
 //     key is the maximum's raw bits as a signed integer with the low 6 bits naming the group)
 //     and sorts them (4 x 19-comparator networks, 3 merges); one merge with the partner
 //     lane gives the token's 8 groups with the largest approximate maxima and the 9th largest.
-//     The token's lane re-scores those 8 groups from global memory (L2; the slot is already
-//     refilled) and keys each group's maximum exactly (exact_sigmoid + bias).  With A8 the
+//     The token's lane reads those 8 groups' logits (fp32: from the tile slot, which the warp
+//     holds until then; 16-bit: from L2, the slot refilled before the sort), re-scores them and
+//     keys each group's maximum exactly (exact_sigmoid + bias).  With A8 the
 //     smallest exact head score, every expert of the exact top 8 has a~ >= A8 - err(A8) =: bound.
 //     If the 9th group maximum is below bound, the exact top 8 is the 8 heads plus the other
 //     elements of the 8 groups that reach bound (typically 0-2), inserted exactly; otherwise
 //     every element of the row that reaches bound is inserted (every element, for a row whose
 //     scores are not all finite): exact, slower.
-//   * Fold: the layer's selection-loss table sits in shared memory as the high 16 bits of each
-//     float (128 KB), a monotone truncation.  The argmin over the retained experts is exact when
-//     the smallest truncated loss is unique and below truncated FLT_MAX; otherwise (ties, values
-//     near FLT_MAX) the fp32 losses are read from global memory.  Scales and confidence losses
-//     are gathered from L2.
+//   * Fold: the argmin over the retained experts of the selection loss (the first minimal loss
+//     below FLT_MAX).  fp32 logits: the fp32 losses are gathered from L2.  16-bit logits: the
+//     layer's loss table sits in shared memory as the high 16 bits of each float (128 KB), a
+//     monotone truncation; the argmin is exact when the smallest truncated loss is unique and
+//     below truncated FLT_MAX, otherwise (ties, values near FLT_MAX) the fp32 losses are read
+//     from global memory.  Scales and confidence losses are gathered from L2.
 #include <float.h>
 
 #include <mutex>
@@ -63,12 +65,19 @@ template <int FOLD, typename LT>
 struct BiasedSmem {
   // 16 KB tiles of fp32 logits (8 KB of bf16 / fp16): the fold's 128 KB table leaves room for 6
   // (12), without it 13 (26)
-  static constexpr int kSlots = (FOLD == kFoldNone ? 13 : 6) * (4 / sizeof(LT));
+  // fp32 logits: the fold's argmins read the fp32 loss table from L2, which leaves 13 tile slots,
+  // and each slot is held until the lane pair has read its token's 8 head groups (65536 tokens,
+  // P = 3, L2 flushed: 49.1 -> 41.0 us; either change alone gains nothing).  16-bit logits: the
+  // table's high halves in shared memory and the heads reloaded from L2 (38.9 us; 43.0 the other
+  // way).
+  static constexpr bool kSmemTable = FOLD != kFoldNone && sizeof(LT) == 2;
+  static constexpr bool kHeadsSmem = sizeof(LT) == 4;
+  static constexpr int kSlots = (kSmemTable ? 6 : 13) * (4 / sizeof(LT));
   // group chunk order of lane t: u ^ (t & kSwz) (16-byte fp32 chunks: quarter-warps, 8-byte
   // 16-bit chunks: half-warps hit distinct banks)
   static constexpr uint32_t kSwz = sizeof(LT) == 4 ? 7u : 15u;
   LT tile[kSlots][kRows * kE];
-  uint16_t loss_hi[FOLD == kFoldNone ? 8 : kE * kE];  // high 16 bits of each loss
+  uint16_t loss_hi[kSmemTable ? kE * kE : 8];  // high 16 bits of each loss
   float cterm[kE];         // 0.5 + bias (rounded), the constant of the approximate score
   float bias[kE];          // the current layer's bias (zeros without one)
   uint64_t bar[kSlots];    // tile copies
@@ -257,7 +266,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
   // use the tile's first token): pk = the token's 8 largest packed maxima, p9 the 9th.  Waits for
   // the tile's copy and refills the slot afterwards; false if a wait timed out.  Warp-uniform.
   auto group_maxima = [&](int64_t k, int rowi, int32_t (&pk)[kK], int32_t& p9,
-                          int32_t& p10) -> bool {
+                          int32_t& p10, bool own, float4 (&xo)[kK]) -> bool {
     const int slot = static_cast<int>(k % kSlots);
     bool ok = !*failed;
     if (ok && t == 0) {
@@ -292,16 +301,18 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
           g[8 * s + i] = static_cast<int32_t>((__float_as_uint(m) & ~63u) | (63u - id));
         }
     }
-    // the tile is consumed: refill its slot with local tile k + kSlots before the sorting
-    // network (generic-proxy reads of the slot are ordered before the bulk copy that overwrites
-    // it)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    if (t == 0 && ok && k + kSlots < nk) {
-      issue(k + kSlots);
-      __threadfence_block();
-      seq[slot] = k + kSlots;
-    }
+    auto refill = [&]() {
+      // the tile is consumed: refill its slot with local tile k + kSlots (generic-proxy reads of
+      // the slot are ordered before the bulk copy that overwrites it)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (t == 0 && ok && k + kSlots < nk) {
+        issue(k + kSlots);
+        __threadfence_block();
+        seq[slot] = k + kSlots;
+      }
+    };
+    if constexpr (!Smem::kHeadsSmem) refill();  // before the sorting network
     p9 = INT32_MIN;
     p10 = INT32_MIN;
 #pragma unroll
@@ -327,7 +338,18 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       p10 = max(p10, o10);
 #pragma unroll
       for (int q = 0; q < kK; ++q) pk[q] = g[q];
+      if (Smem::kHeadsSmem && own) {  // this lane's token: the 8 head groups' logits from the slot
+        const LT* rowp = sm.tile[slot] + rowi * kE;
+#pragma unroll
+        for (int q = 0; q < kK; ++q) {
+          const uint32_t id = 63u - (static_cast<uint32_t>(pk[q]) & 63u);
+          const uint32_t hh = id >> 5, i = id & 31u;
+          const uint32_t osw = (static_cast<uint32_t>(t) & (Smem::kSwz & ~1u)) | hh;
+          xo[q] = load_logits4(rowp + 4 * static_cast<int>(32 * hh + (i ^ osw)));
+        }
+      }
     }
+    if constexpr (Smem::kHeadsSmem) refill();
     return ok;
   };
 
@@ -345,7 +367,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
         sm.bias[e] = b;
         sm.cterm[e] = __fadd_rn(0.5f, b);
       }
-      if (FOLD != kFoldNone) {
+      if (Smem::kSmemTable) {
         // 16 loads in flight per thread before their stores: the 256 KB table costs 4 L2 (or,
         // after L2 was flushed, DRAM) round trips instead of one per few 16-byte vectors
         constexpr int kBatch = 16;
@@ -387,11 +409,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       // Tiles A and B in a loop that is not unrolled (one copy of the group-maxima code: the
       // kernel's instruction fetch was a top stall); each lane keeps its own tile's result.
       int32_t pk[kK] = {}, p9 = INT32_MIN, p10 = INT32_MIN;
+      float4 xq[kK];  // the 8 head groups' logits
       bool ok = true;
 #pragma unroll 1
       for (int which = 0; which < (has_b ? 2 : 1); ++which) {
         int32_t tk[kK], t9 = INT32_MIN, t10 = INT32_MIN;
-        ok = group_maxima(ks + j + which, which ? rb : ra, tk, t9, t10) && ok;
+        ok = group_maxima(ks + j + which, which ? rb : ra, tk, t9, t10,
+                          which == (use_b ? 1 : 0), xq) && ok;
         if (which == (use_b ? 1 : 0)) {
 #pragma unroll
           for (int q = 0; q < kK; ++q) pk[q] = tk[q];
@@ -420,7 +444,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
       float av[kK][4];
       int em[kK];
       int cq[kK];
-      float4 xq[kK];  // the 8 groups' logits, all loads in flight before any use
 #pragma unroll
       for (int q = 0; q < kK; ++q) {
         const uint32_t id = 63u - (pk[q] & 63u);
@@ -428,7 +451,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
         // chunk order of the lane (of this lane's pair) that took the maximum
         const uint32_t osw = (static_cast<uint32_t>(t) & (Smem::kSwz & ~1u)) | hh;
         cq[q] = static_cast<int>(32 * hh + (i ^ osw));
-        xq[q] = ldg_logits4(grow + 4 * cq[q]);
+        if constexpr (!Smem::kHeadsSmem)
+          xq[q] = ldg_logits4(grow + 4 * cq[q]);  // all loads in flight before any use
       }
 #pragma unroll
       for (int q = 0; q < kK; ++q) {
@@ -561,9 +585,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
 #pragma unroll
         for (int j2 = P; j2 < kK; ++j2) {
           const int src = fidx[j2];
+          int pos = 0;
+          if constexpr (!Smem::kSmemTable) {
+            // the fp32 argmin from L2: the first minimal loss below FLT_MAX
+            float lv[P];
+#pragma unroll
+            for (int q = 0; q < P; ++q) lv[q] = __ldg(selg + src * kE + fidx[q]);
+            float bf = FLT_MAX;
+#pragma unroll
+            for (int q = 0; q < P; ++q) {
+              pos = lv[q] < bf ? q : pos;
+              bf = lv[q] < bf ? lv[q] : bf;
+            }
+          } else {
           const uint16_t* lrow = sm.loss_hi + src * kE;
           float hb = __int_as_float(0x7F800000);  // +inf
-          int pos = 0;
           bool tie = false;
 #pragma unroll
           for (int q = 0; q < P; ++q) {
@@ -587,6 +623,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) router_biased_kernel(const Rou
                 pos = q;
               }
             }
+          }
           }
           int tgt = fidx[0];
 #pragma unroll
