@@ -14,15 +14,17 @@
 //     quarter-warp hit 8 different 16-byte bank quads and the reads are conflict-free.  bf16 /
 //     fp16 logits: 8 KB tiles in twice the slots, 8-byte chunks in the order i ^ (t & 15), and
 //     exact group-maximum keys (below), so ties need no fallback.
-//   * Selection keys are IEEE totalOrder keys of the logits.  The 32 groups of 4 consecutive
-//     columns give 32 group maxima; their keys, with the low 5 bits replaced by the group's slot,
-//     go through a sorting network (4 x 19-comparator sorts, 3 merges) whose top 8 name the 8
+//   * The 32 groups of 4 consecutive columns give 32 group maxima (three-input max.f32; for bf16
+//     logits a packed max.bf16x2 first); each is keyed as its raw bits compared as a signed
+//     integer (positive floats rank by value above every negative one), with the low 5 bits
+//     replaced by the group's slot, and the keys go through a sorting network (4 x 19-comparator sorts, 3 merges) whose top 8 name the 8
 //     groups with the largest maxima.  Those groups are reloaded (their exact maxima are then
 //     in descending order unless two truncated keys tie; then they are sorted as (key desc,
 //     column asc)), and every other element of those groups that reaches the 8th maximum is
 //     inserted.  When the 9th largest maximum (the largest value the merges drop) is below the
 //     8th in its truncated key and the 8th maximum is positive, this is the exact top 8 (every
-//     element that reaches it lies in those groups; no zeros, so -0 and +0 cannot tie).  For
+//     element that reaches it lies in those groups; no zeros, so -0 and +0 cannot tie; the named
+//     maxima are then positive floats, compared as floats).  For
 //     16-bit logits the truncation loses nothing and equal keys sort by group, so only the sign
 //     of the 8th maximum and NaN rows decide.  Other
 //     tokens (a group outside the 8 close to the 8th maximum, zeros among the candidates, NaN)
@@ -37,6 +39,7 @@
 #include <float.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "exf_common.cuh"
 #include "exf_kernels.h"
@@ -54,9 +57,10 @@ constexpr int kK = 8;
 #endif
 constexpr int kRows = 32;                // tokens per tile: one per lane
 // Warps per CTA, each ranking one tile at a time.  A warp's tile latency bounds the kernel, so
-// more warps help until the register file (168 registers a thread) runs out: 10 for fp32 logits
-// (12-16 measured slower per launch: they share 10 slots), 14 for 16-bit logits with their
-// 20 slots (21.7 us per 131072-token launch against 23.6 us with 10 warps).
+// more warps help until the register file runs out (registers are allocated per SM sub-partition,
+// so 9-12 warps cap a thread at 168 registers and 13-16 at 128): 10 for fp32 logits (12-16
+// measured slower per launch: they share 10 slots), 14 for 16-bit logits with their 20 slots
+// (21.7 us per 131072-token launch against 23.6 us with 10 warps).
 template <typename LT>
 constexpr int tpt_warps() {
   return sizeof(LT) == 4 ? 10 : 14;
@@ -267,8 +271,19 @@ __global__ void __launch_bounds__(tpt_warps<LT>() * 32, 1) router_tpt_kernel(con
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t grp = static_cast<uint32_t>((8 * s + i) ^ swz);
-            const float4 v = load_logits4(rowp + 4 * grp);
-            const float m = fmax_nan(fmax3_nan(v.x, v.y, v.z), v.w);
+            float m;
+            if constexpr (std::is_same<LT, __nv_bfloat16>::value) {
+              // bf16: the packed maximum of the two pairs, then of its halves (bf16 -> fp32 is
+              // exact and monotone, so this is the maximum of the converted values; NaN
+              // propagates as the canonical NaN)
+              const uint2 u = *reinterpret_cast<const uint2*>(rowp + 4 * grp);
+              uint32_t r2;
+              asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r2) : "r"(u.x), "r"(u.y));
+              m = fmax_nan(__uint_as_float(r2 << 16), __uint_as_float(r2 & 0xFFFF0000u));
+            } else {
+              const float4 v = load_logits4(rowp + 4 * grp);
+              m = fmax_nan(fmax3_nan(v.x, v.y, v.z), v.w);
+            }
             pk[8 * s + i] = static_cast<int32_t>((__float_as_uint(m) & ~31u) |
                                                  (31u - (kExactKeys ? grp : 8 * s + i)));
           }
