@@ -94,6 +94,9 @@ struct DecodeParams {
   int64_t* peers[kMaxPeers];
   int32_t* status;          // set to 1 when a peer's vector did not arrive in time (may be null)
   unsigned long long wait_ns;
+  // set by the launcher: the loss and scale tables are copied into shared memory at the start
+  // (E <= 128, 16-byte aligned tables)
+  int tables_smem;
 };
 
 struct AlignParams {

@@ -7,7 +7,10 @@
  * returns EXF_OK or a negative code; exf_last_error() then holds a message
  * for the calling thread.  No entry point allocates device memory, copies to
  * the host or synchronises: callers own every output and workspace buffer, so
- * the calls can be captured in CUDA graphs.  Calibration tables are fp32,
+ * the calls can be captured in CUDA graphs.  The first launch of a kernel that
+ * uses more than 48 KB of shared memory raises its shared-memory limit once per
+ * device (cudaFuncSetAttribute), so make one eager call of an entry point, with
+ * the shapes it will be captured with, before capturing it.  Calibration tables are fp32,
  * row-major [source][target], `experts` x `experts`.  Routing tensors are
  * row-major [tokens][top_k].
  *
