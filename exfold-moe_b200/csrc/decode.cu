@@ -164,14 +164,20 @@ __device__ __forceinline__ float table_load(const float* t, int64_t i) {
   else return __ldg(t + i);
 }
 template <bool kOnChip>
-__device__ void target_table(const DecodeParams& p, DecodeSmem& sm, const float* loss,
-                             const float* coeff);
+__device__ __forceinline__ void target_table(const DecodeParams& p, DecodeSmem& sm,
+                                             const float* loss, const float* coeff);
 
 template <typename WT, typename IT, bool MERGE = false>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeParams p) {
   __shared__ DecodeSmem sm;
-  extern __shared__ __align__(128) float dtab[];  // [2][E][E]: loss, then coeff (tables_smem)
-  __shared__ uint64_t tab_bar;
+  // [2][E][E] loss, then coeff, then the copies' mbarrier, from the first 128-byte boundary of the
+  // dynamic shared memory (tables_smem; never for MERGE, whose launch has none).  The declared
+  // alignment stays 16 so that the static layout is that of a kernel without the tables (a
+  // 128-byte aligned declaration padded it and measured 4 us slower in the fused layer launch).
+  extern __shared__ __align__(16) float dsm[];
+  float* dtab = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dsm) + 127) &
+                                         ~static_cast<uintptr_t>(127));
+  uint64_t* tab_bar = reinterpret_cast<uint64_t*>(dtab + 2 * p.experts * p.experts);
   const int E = p.experts;
   const int D = p.budget;
   const int tid = threadIdx.x;
@@ -180,28 +186,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   // launched as a programmatic dependent: nothing the previous kernel wrote is read before this
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const bool tsm = p.tables_smem != 0;
+  const bool tsm = !MERGE && p.tables_smem != 0;
   if (tsm && tid == 0) {
     const uint32_t bytes = static_cast<uint32_t>(E) * E * sizeof(float);
-    tile::bar_init(&tab_bar);
+    tile::bar_init(tab_bar);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    tile::bar_expect(&tab_bar, 2 * bytes);
-    tile::bulk_load(dtab, p.loss, bytes, &tab_bar);
-    tile::bulk_load(dtab + E * E, p.coeff, bytes, &tab_bar);
+    tile::bar_expect(tab_bar, 2 * bytes);
+    tile::bulk_load(dtab, p.loss, bytes, tab_bar);
+    tile::bulk_load(dtab + E * E, p.coeff, bytes, tab_bar);
   }
 
   // ---- 1. importance ------------------------------------------------------------------------
   const int copies = kHistLongs / E < 32 ? kHistLongs / E : 32;  // >= 2 for E <= 1024
   long long* hist = sm.hist + ((tid >> 5) % copies) * E;
   const bool from_routes = p.source == kImportanceFromRoutes || p.source == kImportanceExchanged;
-  // the first batch of routes is loaded before the barrier, beside the norms
+  // the first batch of routes is loaded before the barrier, beside the norms, and kept in
+  // registers for phase 4 (not in the decode fused with the expert layer, whose launch measured
+  // 4 us slower per Qwen3 layer with it)
+  constexpr bool kEarly = !MERGE;
   WT wr0[kRouteUnroll];
-  int er0[kRouteUnroll];
-  if (from_routes) {
+  IT raw0[kRouteUnroll];
+  if (kEarly && from_routes) {
 #pragma unroll
     for (int j = 0; j < kRouteUnroll; ++j) {
       const int64_t r = j * kDecodeThreads + tid;
-      er0[j] = r < p.routes ? (int)ids[r] : -1;
+      raw0[j] = r < p.routes ? ids[r] : (IT)-1;
       wr0[j] = r < p.routes ? w[r] : from_f32<WT>(0.0f);
     }
   }
@@ -220,8 +229,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
 #pragma unroll
       for (int j = 0; j < kRouteUnroll; ++j) {
         const int64_t r = base + j * kDecodeThreads + tid;
-        er[j] = base == 0 ? er0[j] : (r < p.routes ? (int)ids[r] : -1);
-        wr[j] = base == 0 ? wr0[j] : (r < p.routes ? w[r] : from_f32<WT>(0.0f));
+        const bool kept = kEarly && base == 0;
+        er[j] = kept ? (int)raw0[j] : (r < p.routes ? (int)ids[r] : -1);
+        wr[j] = kept ? wr0[j] : (r < p.routes ? w[r] : from_f32<WT>(0.0f));
       }
 #pragma unroll
       for (int j = 0; j < kRouteUnroll; ++j) {
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   // (from the shared-memory copies of the tables when their copy has landed; a copy that has
   // not landed within the bounded wait leaves the global tables in use)
   bool on_chip = false;
-  if (tsm) on_chip = __syncthreads_and(tile::bar_wait(&tab_bar, 0) ? 1 : 0) != 0;
+  if (tsm) on_chip = __syncthreads_and(tile::bar_wait(tab_bar, 0) ? 1 : 0) != 0;
   if (on_chip)
     target_table<true>(p, sm, dtab, dtab + E * E);
   else
@@ -302,8 +312,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
 #pragma unroll
     for (int j = 0; j < kRouteUnroll; ++j) {
       const int64_t r = base + j * kDecodeThreads + tid;
-      raw[j] = r < p.routes ? ids[r] : (IT)-1;
-      wr[j] = r < p.routes ? w[r] : from_f32<WT>(0.0f);
+      const bool kept = kEarly && from_routes && base == 0;  // loaded in phase 1
+      raw[j] = kept ? raw0[j] : (r < p.routes ? ids[r] : (IT)-1);
+      wr[j] = kept ? wr0[j] : (r < p.routes ? w[r] : from_f32<WT>(0.0f));
     }
 #pragma unroll
     for (int j = 0; j < kRouteUnroll; ++j) {
@@ -331,12 +342,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeP
   }
   if constexpr (MERGE) merge_routes<WT, IT>(p);
   // a table copy still in flight after a timed-out wait lands before the shared memory is freed
-  if (tsm && !on_chip && tid == 0) tile::bar_wait(&tab_bar, 0);
+  if (tsm && !on_chip && tid == 0) tile::bar_wait(tab_bar, 0);
 }
 
 template <bool kOnChip>
-__device__ void target_table(const DecodeParams& p, DecodeSmem& sm, const float* loss,
-                             const float* coeff) {
+__device__ __forceinline__ void target_table(const DecodeParams& p, DecodeSmem& sm,
+                                             const float* loss, const float* coeff) {
   const int E = p.experts;
   const int D = p.budget;
   const int tid = threadIdx.x;
@@ -580,12 +591,12 @@ static bool tables_fit(const DecodeParams& p) {
 template <typename WT, typename IT, bool MERGE = false>
 static cudaError_t launch_decode_t(const DecodeParams& pin, cudaStream_t s) {
   auto kern = decode_kernel<WT, IT, MERGE>;
-  constexpr size_t kMaxTables = 2 * kSmemTableExperts * kSmemTableExperts * sizeof(float);
+  constexpr size_t kMaxTables = 2 * kSmemTableExperts * kSmemTableExperts * sizeof(float) + 144;
   static std::mutex mu;
   static bool allowed[64] = {};
   DecodeParams p = pin;
-  // (not for the decode fused with the expert layer: its 158 KB CTA measured 2.4 us slower per
-  // Qwen3 layer there, 139.4 -> 141.9 us; the plain 48-layer decode gains 13.41 -> 13.10 us)
+  // (not for the decode fused with the expert layer, whose launch measured slower with it; the
+  // plain 48-layer decode, with the first routes kept in registers, 13.40 -> 12.88 us per layer)
   p.tables_smem = !MERGE && tables_fit(p) ? 1 : 0;
   if (p.tables_smem) {
     int dev = 0;
@@ -604,7 +615,7 @@ static cudaError_t launch_decode_t(const DecodeParams& pin, cudaStream_t s) {
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes =
-      p.tables_smem ? 2 * static_cast<size_t>(p.experts) * p.experts * sizeof(float) : 0;
+      p.tables_smem ? 2 * static_cast<size_t>(p.experts) * p.experts * sizeof(float) + 144 : 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
