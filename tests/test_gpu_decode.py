@@ -149,6 +149,34 @@ def test_decode_dtypes_and_sizes(variant, wdtype, idtype):
             np.testing.assert_allclose(got, ref, rtol=2 ** -7, atol=0)
 
 
+@pytest.mark.parametrize("variant", ["qwen3", "dsv4"])
+def test_decode_table_paths(variant):
+    """The decode reads its tables from shared memory at E <= 128 (even E, 16-byte aligned
+    tables) and from L2 otherwise; both, and batches of more than one 8192-route load batch,
+    equal the oracle bit for bit."""
+    cases = ((128, 1500, 64), (96, 300, 40), (127, 200, 50), (128, 1024, 64))
+    for n, (experts, batch, budget) in enumerate(cases):
+        lay = W.Layer(seed=1700 + n, tokens=batch, experts=experts, top_k=8, kind="qwen3")
+        rw, ri = O.router_topk(lay.logits, 8, "softmax")
+        coeff, loss = cuda(lay.coeff), cuda(lay.loss)
+        if n == 3:  # tables 4 bytes off a 16-byte boundary: the L2 path at E = 128
+            cbuf = torch.zeros(experts * experts + 1, device=DEV)
+            lbuf = torch.zeros(experts * experts + 1, device=DEV)
+            cbuf[1:] = coeff.reshape(-1)
+            lbuf[1:] = loss.reshape(-1)
+            coeff = cbuf[1:].view(experts, experts)
+            loss = lbuf[1:].view(experts, experts)
+            assert coeff.data_ptr() % 16 != 0 and loss.data_ptr() % 16 != 0
+        ow, oi = ops.decode(cuda(rw), cuda(ri), cuda(lay.norms), coeff, loss, budget,
+                            variant=variant)
+        if variant == "qwen3":
+            ew, ei, _ = O.decode_qwen3(rw, ri, lay.norms, lay.coeff, lay.loss, budget)
+        else:
+            ew, ei = O.decode_dsv4(rw, ri, lay.norms, lay.coeff, lay.loss, budget)
+        np.testing.assert_array_equal(host(oi), ei)
+        np.testing.assert_array_equal(host(ow), ew)
+
+
 def test_split_decode_equals_fused():
     """importance on shards + summed vector + apply == one fused decode (bit for bit)."""
     lay = W.layer("qwen3_layers", tokens=1024, layer_index=3)
